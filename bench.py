@@ -1,0 +1,417 @@
+#!/usr/bin/env python
+"""Throughput of the implicitly zero-padded real 2D FFT cross-correlation.
+
+Workload (one "step"): a 4096 x 4096 float32 image (N(0,1), seed 0) given by
+its precomputed, transposed spectrum (2049 x 4096 complex64, computed once,
+untimed); a batch of 32 templates of 256 x 256 (N(0,1) times a soft circular
+mask of radius 120 px, then zero-mean / unit-variance; seed 1 + rank); the
+full 32 x 4096 x 4096 float32 correlation maps.  One process per GPU, every
+rank correlates its own batch (weak scaling, no data-path collective).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl zipfft|reference]
+
+Prints one JSON line on rank 0.  `value` times K steps with the inputs
+resident in HBM; `e2e` times K steps through zipfft.padded_rconv2d.corr with
+the templates copied from pinned host memory and each template's peak score
+read back every step.  `--impl reference` times the reference's own
+correctness path (torch.fft on the host CPU, mgiammar/zipFFT
+tests/test_real_conv_2d.py:110-123) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "2D padded cross-corr/sec at 4096² img, 256² tmpl; % HBM roofline; 1/2/4/8 GPU"
+UNIT = "corr/s"
+H = W = 4096
+TH = TW = 256
+BATCH = 32
+# Minimum bytes per correlation: fp32 template + c64 image spectrum + fp32 output.
+ALG_BYTES = TH * TW * 4 + H * (W // 2 + 1) * 8 + H * W * 4  # 134,512,640
+L2_NOTE = ("no L2 flush: every step streams 32 x 67 MB of spectrum reads and "
+           "2.1 GB of output writes through the 126 MB L2")
+WORKLOAD = ("4096^2 f32 image (spectrum precomputed) x 32 soft-masked 256^2 f32 templates "
+            "per GPU, full 4096^2 maps")
+
+
+def soft_mask(n: int = TH, r_in: float = 112.0, r_out: float = 120.0) -> torch.Tensor:
+    """1 inside r_in, raised cosine to 0 at r_out, centred at ((n-1)/2, (n-1)/2)."""
+    c = (n - 1) / 2.0
+    yy, xx = torch.meshgrid(torch.arange(n, dtype=torch.float64),
+                            torch.arange(n, dtype=torch.float64), indexing="ij")
+    r = torch.sqrt((yy - c) ** 2 + (xx - c) ** 2)
+    m = torch.where(r <= r_in, torch.ones_like(r),
+                    torch.where(r >= r_out, torch.zeros_like(r),
+                                0.5 * (1 + torch.cos(math.pi * (r - r_in) / (r_out - r_in)))))
+    return m.float()
+
+
+def make_templates(n: int, seed: int) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    t = torch.randn((n, TH, TW), generator=g) * soft_mask()[None]
+    t = t - t.mean(dim=(1, 2), keepdim=True)
+    return (t / t.std(dim=(1, 2), keepdim=True)).contiguous()
+
+
+def make_image(seed: int = 0) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    return torch.randn((H, W), generator=g)
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, smax, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(nm)
+        loaded = [s for s in sm if smax and s > 0.3 * smax] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing (one process per GPU; timing only, no data collectives)
+# ---------------------------------------------------------------------------
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's torch.fft path on the host cores
+# ---------------------------------------------------------------------------
+def cpu_reference_rate(min_seconds: float = 10.0, templates_per_sample: int = 2):
+    from oracle import xcorr_oracle as O
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    image_fft = torch.fft.rfftn(make_image(0))
+    tm = make_templates(templates_per_sample, 1)
+    O.reference_torch_path(tm[:1], image_fft, H, W, True, True)  # warm the FFT plans
+    n, t0 = 0, time.perf_counter()
+    while True:
+        O.reference_torch_path(tm, image_fft, H, W, True, True)
+        n += templates_per_sample
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    return n / el, cores, n, el
+
+
+def run_reference_arm(args, world, rank):
+    if rank != 0:
+        return 0
+    from oracle import xcorr_oracle as O
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    image_fft = torch.fft.rfftn(make_image(0))
+    per_step = 2
+    tm = make_templates(per_step, 1)
+    for _ in range(args.warmup):
+        O.reference_torch_path(tm, image_fft, H, W, True, True)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.reference_torch_path(tm, image_fft, H, W, True, True)
+    el = time.perf_counter() - t0
+    value = per_step * args.steps / el
+    sample = (f"{per_step} of the 32 templates per step (4096^2 full maps), "
+              f"torch.fft on {cores} host threads")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": WORKLOAD, "image": [H, W],
+                                        "template": [TH, TW], "templates_per_step": per_step,
+                                        "output": "full"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def cufft_torch_rate(spec_nat, tm_dev, steps=5, warmup=2):
+    """The explicit-pad torch.fft (cuFFT) pipeline on the same GPU, for comparison."""
+    import torch.nn.functional as F
+
+    def step():
+        pad = F.pad(tm_dev, (0, W - TW, 0, H - TH))
+        f = torch.fft.rfft2(pad)
+        return torch.fft.irfft2(spec_nat[None] * torch.conj(f), s=(H, W))
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        out = step()
+    e.record()
+    torch.cuda.synchronize()
+    del out
+    ms = s.elapsed_time(e) / steps
+    return BATCH / (ms / 1e3), ms
+
+
+def run_gpu_arm(args, world, rank, local):
+    import zipfft
+    from zipfft_b200 import _lib
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    image = make_image(0).to(dev)
+    spec_nat = torch.fft.rfftn(image)                 # setup only (untimed)
+    spec_T = spec_nat.transpose(0, 1).contiguous()    # (W/2+1, H) as the API expects
+    tm_host = make_templates(BATCH, 1 + rank).pin_memory()
+    tm = tm_host.to(dev)
+    ws = torch.empty((BATCH, H, W // 2 + 1), dtype=torch.complex64, device=dev)
+    out = torch.empty((BATCH, H, W), dtype=torch.float32, device=dev)
+
+    def step():
+        zipfft.padded_rconv2d.corr(tm, ws, spec_T, out, H, W)
+
+    # ---- device-resident throughput --------------------------------------
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    torch.cuda.synchronize()
+    barrier(world)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    ms_total = max_over_ranks(ev0.elapsed_time(ev1), world)
+    ms_step = ms_total / args.steps
+    value = world * BATCH * args.steps / (ms_total / 1e3)
+
+    # ---- per-kernel device time (separate instrumented steps) -------------
+    _lib.stage_timing(True)
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize()
+    stages = _lib.stage_timing_read()
+    _lib.stage_timing(False)
+    kern = {}
+    tot_ms = sum(v[0] for v in stages.values())
+    for name, (ms, n) in stages.items():
+        kern[name] = {"launches": n, "ms_per_launch": ms / max(n, 1),
+                      "share": ms / tot_ms if tot_ms else None}
+
+    # ---- end to end through the public API with host buffers --------------
+    peaks_host = torch.empty((BATCH,), dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        tm.copy_(tm_host, non_blocking=True)
+        zipfft.padded_rconv2d.corr(tm, ws, spec_T, out, H, W)
+        peaks_host.copy_(torch.amax(out, dim=(1, 2)), non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+    e2e_value = world * BATCH * args.steps / (e2e_ms / 1e3)
+
+    # ---- comparison and baselines (rank 0, N = 1) --------------------------
+    cufft = cpu = None
+    if rank == 0 and world == 1 and not args.skip_baselines:
+        rate, ms = cufft_torch_rate(spec_nat, tm)
+        cufft = {"value": rate, "unit": UNIT, "ms_per_step": ms,
+                 "pipeline": "F.pad + torch.fft.rfft2 + *conj + irfft2 (cuFFT), same GPU"}
+        rate, cores, n, el = cpu_reference_rate()
+        cpu = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": f"{n} templates of this workload (4096^2 full maps) in {el:.1f} s, "
+                         f"the reference test's torch.fft path (oracle) on {cores} host threads"}
+
+    if rank == 0:
+        per_gpu = value / world
+        achieved = ALG_BYTES * per_gpu / 1e9
+        peak, peak_src = measured_hbm_peak()
+        traffic = measured_traffic()
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1) image and soft-masked templates)",
+            "config": {"workload": WORKLOAD, "image": [H, W], "template": [TH, TW],
+                       "templates_per_gpu_step": BATCH, "global_batch": BATCH * world,
+                       "output": "full", "parallelism": f"dp{world} (template shards)",
+                       "l2": L2_NOTE},
+            "e2e": {"value": e2e_value, "unit": UNIT,
+                    "h2d_bytes_per_step": BATCH * TH * TW * 4,
+                    "d2h_bytes_per_step": BATCH * 4,
+                    "api": "zipfft.padded_rconv2d.corr; templates copied from pinned host "
+                           "memory, per-template peak score read back each step"},
+            "gpu_launches": 3 * BATCH * args.steps,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "unit_of_work": "one correlation (k_row_r2c + k_col_fused + k_row_c2r "
+                                         "for one template)",
+                         "algorithmic_bytes_per_unit": ALG_BYTES, "peak_source": peak_src},
+            "kernels": kern,
+            "clocks": clk,
+        }
+        if cufft is not None:
+            line["cufft_torch"] = cufft
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def measured_hbm_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "MEASURED_PEAKS.json hbm_gbs (of measured)"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback 6.65 TB/s (of fallback)"
+
+
+def measured_traffic():
+    """DRAM bytes (read + write) per correlation from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "dram_traffic.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["dram_bytes_per_correlation"])
+    except (OSError, KeyError, ValueError):
+        return None
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__,
+                                 formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("zipfft", "reference"), default="zipfft")
+    ap.add_argument("--skip-baselines", action="store_true",
+                    help="skip the cuFFT comparison and the CPU baseline")
+    args = ap.parse_args(argv)
+    args.warmup = max(args.warmup, 3)  # at least 3 untimed warm-up steps; reported as run
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        return run_reference_arm(args, world, rank)
+    world, rank, local = dist_setup()
+    try:
+        return run_gpu_arm(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

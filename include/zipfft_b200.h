@@ -1,0 +1,106 @@
+/* C ABI of libzipfft_b200.so: implicitly zero-padded real 2D FFT
+ * convolution / cross-correlation on NVIDIA B200 (sm_100a).
+ *
+ * Every entry point takes plain pointers and sizes, launches asynchronously on
+ * the given CUDA stream (a cudaStream_t passed as void*; NULL is the legacy
+ * default stream) of the given device, and returns a status code.  On a
+ * non-zero status zfft_get_last_error() describes the failure (per calling
+ * thread).  Nothing here allocates device memory: all buffers are the
+ * caller's.  The first call on a device uploads the twiddle tables (a
+ * synchronous copy); make that first call outside CUDA graph capture.
+ *
+ * Reference interface replaced (mgiammar/zipFFT):
+ *   src/cuda/real_conv_2d_binding.cu:288-299  conv / corr   (pybind11, torch::Tensor)
+ *   src/cuda/real_conv_2d_binding.cu:189-285  padded_real_conv_2d_impl (validation + dispatch)
+ *   src/cuda/real_conv_2d_binding.cu:160-170  get_supported_conv_configs
+ *   src/cuda/real_conv_2d.cuh:296-335         padded_block_real_conv_2d (launcher)
+ */
+#ifndef ZIPFFT_B200_H_
+#define ZIPFFT_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ZFFT_API __attribute__((visibility("default")))
+#else
+#define ZFFT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ZFFT_SUCCESS 0
+#define ZFFT_ERROR_INVALID_VALUE 1 /* bad shape, pointer, size or alignment */
+#define ZFFT_ERROR_UNSUPPORTED 2   /* FFT size not built into the library */
+#define ZFFT_ERROR_CUDA 3          /* CUDA runtime error (launch, device) */
+#define ZFFT_ERROR_TIMEOUT 4       /* a bounded device-side wait gave up */
+
+/* Padded real 2D convolution (conv) and cross-correlation (corr) of a batch of
+ * small real templates with one large real image given by its spectrum.
+ * Replaces zipfft.padded_rconv2d.conv / .corr (real_conv_2d_binding.cu:288-299).
+ *
+ *   input         float32 [batch][signal_y][signal_x], contiguous
+ *   fft_workspace complex64 scratch; at least zfft_workspace_bytes(fft_y, fft_x)
+ *                 bytes (one (fft_y, fft_x/2 + 1) slice, as in the reference,
+ *                 is always enough).  Clobbered.
+ *   conv_data     complex64 [fft_x/2 + 1][fft_y]: rfft2 of the image, transposed
+ *                 (the reference's pre-transposed layout, binding.cu:248-255)
+ *   output        float32 [batch][output_y][output_x] where (output_y, output_x)
+ *                 is either the valid crop (fft_y - signal_y + 1,
+ *                 fft_x - signal_x + 1) as in the reference, or the full
+ *                 circular map (fft_y, fft_x)
+ *   fft_size_y/x  image size H, W (zfft_is_fft_size_supported)
+ *
+ * corr computes out[u][v] = sum_{y,x} T[y][x] I[(y+u) mod H][(x+v) mod W],
+ * conv computes out[u][v] = sum_{y,x} T[y][x] I[(u-y) mod H][(v-x) mod W]
+ * (torch.fft.irfftn(rfftn(I) * conj(rfftn(T, s=(H, W)))) and its unconjugated
+ * form, norm="backward").  batch == 0 is a no-op. */
+ZFFT_API int zfft_padded_real_corr_2d(const float* input, int batch, int signal_y, int signal_x,
+                             void* fft_workspace, size_t fft_workspace_bytes,
+                             const void* conv_data, float* output, int output_y, int output_x,
+                             int fft_size_y, int fft_size_x, int device, void* stream);
+
+ZFFT_API int zfft_padded_real_conv_2d(const float* input, int batch, int signal_y, int signal_x,
+                             void* fft_workspace, size_t fft_workspace_bytes,
+                             const void* conv_data, float* output, int output_y, int output_x,
+                             int fft_size_y, int fft_size_x, int device, void* stream);
+
+/* Bytes of fft_workspace the two calls above need for an (fft_y, fft_x)
+ * image: fft_y * (fft_x / 2) complex64 values, independent of the batch
+ * (templates are processed one after another through the same slice).
+ * Returns 0 for unsupported sizes.  No counterpart in the reference, which
+ * sizes the workspace (batch, fft_y, fft_x/2 + 1) (binding.cu:235-245). */
+ZFFT_API size_t zfft_workspace_bytes(int fft_size_y, int fft_size_x);
+
+/* 1 if n is a supported FFT size (for H and W), else 0.  Replaces the
+ * compile-time shape table's size check (binding.cu:51-106). */
+ZFFT_API int zfft_is_fft_size_supported(int n);
+
+/* Validated configurations as 6-int records (signal_y, signal_x, fft_y, fft_x,
+ * batch, cross_correlate); writes at most `capacity` records and returns the
+ * total count.  Replaces get_supported_conv_configs (binding.cu:160-170). */
+ZFFT_API int zfft_get_supported_conv_configs(int* records, int capacity);
+
+/* Description of the last failure on the calling thread ("" if none). */
+ZFFT_API const char* zfft_get_last_error(void);
+
+/* Per-stage device timing for benchmarks (no counterpart in the reference,
+ * whose benchmark times whole calls: benchmark/run_benchmark.cu:364-379).
+ * While enabled on the calling thread, every kernel launch of the calls above
+ * is bracketed by CUDA events on the call's stream.  zfft_stage_timing_read
+ * waits for those events and writes, for stage 0 (row r2c), 1 (fused column)
+ * and 2 (row c2r), the summed milliseconds and launch counts (arrays of n >= 3
+ * entries), then clears the record. */
+ZFFT_API int zfft_stage_timing_enable(int enable);
+ZFFT_API int zfft_stage_timing_read(double* ms, int* launches, int n);
+
+/* Library version as major * 10000 + minor * 100 + patch. */
+ZFFT_API int zfft_get_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ZIPFFT_B200_H_ */

@@ -1,0 +1,157 @@
+"""Parity of the CUDA path with the CPU oracle, through the C ABI.
+
+Seeded inputs, the oracle (oracle/xcorr_oracle.py, float64) on the same
+complex64 image spectrum the kernels receive, and the tolerances of the
+reference test (rel L2 < 5e-6, test:173-174) and the 2DTM requirement
+(max |err| < 1e-4 x peak).  Full-size 2DTM workloads are checked on sampled
+templates against the oracle and on all templates through size-independent
+properties (linearity in the template, a planted template's correlation peak).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import xcorr_oracle as O
+from tests.gpu_helpers import assert_parity, capi_corr, make_inputs
+
+pytestmark = pytest.mark.gpu
+
+
+def test_golden_fixtures_through_capi(golden):
+    for name, c in golden.items():
+        B, sy, sx, H, W, conj, full = (int(v) for v in c["meta"])
+        out = capi_corr(torch.from_numpy(c["templates"]), torch.from_numpy(c["spec_T"]), H, W,
+                        bool(full), bool(conj))
+        assert_parity(c["torch"], out, what=name + " vs reference torch path")
+        assert_parity(c["direct"], out, what=name + " vs direct sum")
+
+
+SMALL = [
+    # B, sy, sx, H, W, conj, full
+    (3, 16, 16, 64, 64, True, True),
+    (2, 48, 48, 64, 64, False, False),
+    (1, 64, 64, 64, 64, True, True),        # no padding at all
+    (2, 1, 1, 128, 128, True, True),        # single-pixel template
+    (2, 7, 13, 128, 256, True, False),      # odd template sizes
+    (2, 31, 9, 256, 512, False, True),
+    (1, 200, 100, 512, 256, True, False),
+    (2, 100, 100, 1024, 1024, True, True),
+    (2, 127, 255, 2048, 1024, True, False),
+    (1, 3, 5, 120, 240, True, True),        # radix-3/5 sizes
+    (2, 60, 90, 480, 960, False, True),
+    (1, 500, 300, 1920, 3840, True, False),
+    (1, 256, 128, 4096, 2048, True, True),  # pruned start, nz = 1
+    (1, 384, 384, 4096, 4096, True, True),  # pruned start, nz = 2
+    (1, 700, 600, 4096, 4096, False, False),  # full start
+]
+
+
+@pytest.mark.parametrize("case", SMALL, ids=[str(c) for c in SMALL])
+def test_seeded_parity(case):
+    B, sy, sx, H, W, conj, full = case
+    _, tm, spec = make_inputs(B, sy, sx, H, W, seed=sum(case[:5]))
+    out = capi_corr(tm, spec, H, W, full, conj)
+    ref = O.padded_corr2d_f64(tm.numpy(), spec.numpy(), H, W, conj, full)
+    assert_parity(ref, out, what=str(case))
+
+
+def test_config1_1024_full_maps():
+    """1024^2 image, 4 templates 128^2 N(0,1) zero-mean unit-variance, full maps."""
+    g = torch.Generator().manual_seed(0)
+    img = torch.randn((1024, 1024), generator=g)
+    tm = torch.randn((4, 128, 128), generator=g)
+    tm = (tm - tm.mean(dim=(1, 2), keepdim=True)) / tm.std(dim=(1, 2), keepdim=True)
+    spec = torch.from_numpy(O.image_spectrum_T(img.numpy()))
+    out = capi_corr(tm, spec, 1024, 1024, True)
+    ref = O.padded_corr2d_f64(tm.numpy(), spec.numpy(), 1024, 1024, True, True)
+    assert_parity(ref, out, what="1024^2 x 4 x 128^2")
+
+
+@pytest.mark.parametrize("H,h,B,check", [(4096, 256, 32, (0, 17, 31)), (4096, 512, 8, (0, 7)),
+                                         (3840, 384, 8, (0, 5))])
+def test_2dtm_sizes_sampled_templates(H, h, B, check):
+    _, tm, spec = make_inputs(B, h, h, H, H, seed=H + h)
+    out = capi_corr(tm, spec, H, H, True)
+    for b in check:
+        ref = O.padded_corr2d_f64(tm[b].numpy(), spec.numpy(), H, H, True, True)
+        assert_parity(ref, out[b], what=f"{H}^2 / {h}^2 template {b}")
+
+
+def test_linearity_full_size():
+    """corr(a T1 + b T2) = a corr(T1) + b corr(T2) at 4096^2 / 256^2."""
+    H = 4096
+    _, tm, spec = make_inputs(2, 256, 256, H, H, seed=11)
+    a, b = 0.75, -1.25
+    mix = (a * tm[0] + b * tm[1])[None]
+    both = capi_corr(torch.cat([tm, mix]), spec, H, H, True)
+    lhs = both[2].astype(np.float64)
+    rhs = a * both[0].astype(np.float64) + b * both[1].astype(np.float64)
+    assert O.rel_l2(lhs, rhs) < 5e-6
+
+
+def test_planted_template_peak_full_size():
+    """A template added to the image at known offsets gives correlation peaks
+    exactly there (the known answer of 2D template matching)."""
+    H = 4096
+    rng = np.random.default_rng(5)
+    img = rng.standard_normal((H, H)).astype(np.float32)
+    t = rng.standard_normal((256, 256)).astype(np.float32)
+    pos = [(100, 200), (3000, 1500), (4000 - 256, 17)]
+    for (y, x) in pos:
+        img[y:y + 256, x:x + 256] += 2.0 * t
+    spec = torch.from_numpy(O.image_spectrum_T(img))
+    out = capi_corr(torch.from_numpy(t)[None], spec, H, H, True)[0]
+    flat = np.argsort(out.ravel())[::-1][:3]
+    found = sorted((int(i // H), int(i % H)) for i in flat)
+    assert found == sorted(pos)
+
+
+def test_workspace_only_needs_one_slice_and_output_untouched_beyond():
+    """The kernels stay inside H * W/2 complex of workspace and the output
+    tensor; guard regions around both remain intact."""
+    H = W = 1024
+    _, tm, spec = make_inputs(3, 64, 64, H, W, seed=3)
+    dev = torch.device("cuda", 0)
+    nws = H * (W // 2)
+    guard = 4096
+    ws_all = torch.full((nws + 2 * guard,), complex(7.0, -7.0), dtype=torch.complex64, device=dev)
+    ws = ws_all[guard:guard + nws]
+    out = capi_corr(tm, spec, H, W, False, ws=ws)
+    torch.cuda.synchronize()
+    assert torch.all(ws_all[:guard] == complex(7.0, -7.0))
+    assert torch.all(ws_all[guard + nws:] == complex(7.0, -7.0))
+    ref = O.padded_corr2d_f64(tm.numpy(), spec.numpy(), H, W, True, False)
+    assert_parity(ref, out, what="guarded workspace")
+
+
+def test_convolution_matches_oracle_large():
+    _, tm, spec = make_inputs(2, 256, 256, 4096, 4096, seed=21)
+    out = capi_corr(tm, spec, 4096, 4096, True, conj=False)
+    ref = O.padded_corr2d_f64(tm[1].numpy(), spec.numpy(), 4096, 4096, False, True)
+    assert_parity(ref, out[1], what="conv 4096^2 / 256^2")
+
+
+def test_results_independent_of_stream_and_repeatable():
+    _, tm, spec = make_inputs(4, 96, 96, 512, 512, seed=9)
+    s = torch.cuda.Stream()
+    a = capi_corr(tm, spec, 512, 512, True)
+    with torch.cuda.stream(s):
+        b = capi_corr(tm, spec, 512, 512, True, stream=s.cuda_stream)
+    assert np.array_equal(a, b)  # deterministic: no atomics, fixed schedule
+
+
+def test_invalid_device_index_reports_error():
+    from zipfft_b200 import _lib
+
+    lib = _lib.load()
+    n = torch.cuda.device_count()
+    # Correctly sized buffers: even if validation let the call through, every
+    # access would stay in bounds.
+    x = torch.zeros(16, 16, device="cuda")
+    ws = torch.zeros(64 * 33, dtype=torch.complex64, device="cuda")
+    cd = torch.zeros(33, 64, dtype=torch.complex64, device="cuda")
+    out = torch.zeros(64, 64, device="cuda")
+    st = lib.zfft_padded_real_corr_2d(x.data_ptr(), 1, 16, 16, ws.data_ptr(), ws.numel() * 8,
+                                      cd.data_ptr(), out.data_ptr(), 64, 64, 64, 64, n + 3, None)
+    assert st == _lib.ZFFT_ERROR_INVALID_VALUE
+    assert "invalid device index" in _lib.last_error()

@@ -1,0 +1,360 @@
+// extern "C" entry points of libzipfft_b200.so (declared in include/zipfft_b200.h).
+//
+// Mirrors the validation and dispatch of zipFFT's binding
+// (src/cuda/real_conv_2d_binding.cu:189-285) and launcher
+// (src/cuda/real_conv_2d.cuh:153-293) with these differences:
+//   * shapes are run-time values (only the FFT sizes are compiled in);
+//   * errors are returned as status codes with a message, never std::exit
+//     (zipfft_common.hpp:20-41) and never silently ignored (binding.cu:284);
+//   * the output may be the valid crop (as the reference) or the full map;
+//   * the per-call cudaFuncSetAttribute / workspace creation of the reference
+//     (cuh:243-259) happen once per device.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/zipfft_b200.h"
+#include "fft_core.cuh"
+#include "launch.h"
+
+namespace {
+
+constexpr int kVersion = 100;  // 0.1.0
+constexpr int kMaxDevices = 64;
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(ZFFT_ERROR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+// ---------------------------------------------------------------------------
+// Twiddle tables: w_N[m] = exp(-2 pi i m / N), one table per supported size,
+// computed in double precision on the host and uploaded once per device.
+// ---------------------------------------------------------------------------
+__device__ float2 g_tw_pool[ZF_TW_POOL_TOTAL];
+
+int tw_offset(int n) {
+    int off = 0;
+#define ZF_X(N)              \
+    if (n == (N)) return off; \
+    off += (N);
+    ZF_FOR_EACH_FFT_SIZE(ZF_X)
+#undef ZF_X
+    return -1;
+}
+
+std::mutex g_init_mu;
+bool g_dev_ready[kMaxDevices];
+float2* g_dev_pool[kMaxDevices];
+
+int ensure_device(int device) {
+    std::lock_guard<std::mutex> lock(g_init_mu);
+    if (g_dev_ready[device]) return ZFFT_SUCCESS;
+    std::vector<float2> host(ZF_TW_POOL_TOTAL);
+#define ZF_X(N)                                                      \
+    {                                                                \
+        const int o = tw_offset(N);                                  \
+        for (int m = 0; m < (N); ++m) {                              \
+            const double a = 2.0 * zf::kPi * double(m) / double(N);  \
+            host[o + m].x = float(std::cos(a));                      \
+            host[o + m].y = float(-std::sin(a));                     \
+        }                                                            \
+    }
+    ZF_FOR_EACH_FFT_SIZE(ZF_X)
+#undef ZF_X
+    cudaError_t e = cudaMemcpyToSymbol(g_tw_pool, host.data(), sizeof(float2) * host.size());
+    if (e != cudaSuccess) return cuda_fail(e, "uploading twiddle tables");
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_tw_pool);
+    if (e != cudaSuccess) return cuda_fail(e, "resolving twiddle table address");
+    g_dev_pool[device] = static_cast<float2*>(p);
+    g_dev_ready[device] = true;
+    return ZFFT_SUCCESS;
+}
+
+// RAII: make `device` current for the call, restore the caller's device.
+struct DeviceGuard {
+    int prev = -1;
+    cudaError_t err = cudaSuccess;
+    explicit DeviceGuard(int device) {
+        err = cudaGetDevice(&prev);
+        if (err == cudaSuccess && prev != device) err = cudaSetDevice(device);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+bool supported(int n) { return tw_offset(n) >= 0; }
+
+// ---------------------------------------------------------------------------
+// Opt-in per-stage timing for benchmarks: while enabled on the calling thread,
+// events are recorded on the call's stream around every kernel launch, and
+// zfft_stage_timing_read sums their intervals per stage.
+// ---------------------------------------------------------------------------
+constexpr int kStages = 3;  // 0: row r2c, 1: column, 2: row c2r
+struct StageTimer {
+    bool on = false;
+    int device = -1;
+    std::vector<cudaEvent_t> pool;      // reusable events
+    std::vector<std::pair<int, int>> marks[kStages];  // (start, stop) indices into pool
+    size_t used = 0;
+    cudaEvent_t next(cudaError_t* e) {
+        if (used == pool.size()) {
+            cudaEvent_t ev;
+            *e = cudaEventCreate(&ev);
+            if (*e != cudaSuccess) return nullptr;
+            pool.push_back(ev);
+        }
+        return pool[used++];
+    }
+};
+thread_local StageTimer g_timer;
+
+// Record the start of a stage launch; returns the pool index (or -1).
+int timer_mark(cudaStream_t s) {
+    if (!g_timer.on) return -1;
+    cudaError_t e = cudaSuccess;
+    cudaEvent_t ev = g_timer.next(&e);
+    if (!ev || cudaEventRecord(ev, s) != cudaSuccess) return -1;
+    return int(g_timer.used - 1);
+}
+void timer_close(int stage, int start, cudaStream_t s) {
+    if (start < 0) return;
+    int stop = timer_mark(s);
+    if (stop >= 0) g_timer.marks[stage].push_back({start, stop});
+}
+
+using ColFn = cudaError_t (*)(float2*, const float2*, const float2*, int, int, int, bool, int, int,
+                              cudaStream_t);
+using R2cFn = cudaError_t (*)(const float*, float2*, const float2*, int, int, int, float, int, int,
+                              cudaStream_t);
+using C2rFn = cudaError_t (*)(const float2*, float*, const float2*, int, int, int, int, int,
+                              cudaStream_t);
+
+ColFn col_fn(int n) {
+#define ZF_X(N) \
+    if (n == (N)) return zf::launch_col_##N;
+    ZF_FOR_EACH_FFT_SIZE(ZF_X)
+#undef ZF_X
+    return nullptr;
+}
+R2cFn r2c_fn(int n) {
+#define ZF_X(N) \
+    if (n == (N)) return zf::launch_row_r2c_##N;
+    ZF_FOR_EACH_FFT_SIZE(ZF_X)
+#undef ZF_X
+    return nullptr;
+}
+C2rFn c2r_fn(int n) {
+#define ZF_X(N) \
+    if (n == (N)) return zf::launch_row_c2r_##N;
+    ZF_FOR_EACH_FFT_SIZE(ZF_X)
+#undef ZF_X
+    return nullptr;
+}
+
+// Number of possibly non-zero inputs per stage-0 butterfly of an n-point
+// transform whose first `len` inputs are non-zero: 1, 2 or 0 (= more).
+int stage0_nz(int n, int len) {
+    const int nb0 = n / zf::plan_first_radix(n);
+    const int nz = (len + nb0 - 1) / nb0;
+    return nz <= 2 ? (nz < 1 ? 1 : nz) : 0;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// zipFFT's compile-time shape table (real_conv_2d_binding.cu:51-106) -- every
+// entry runs here -- followed by the 2DTM shapes this library is measured on.
+const int kConfigs[][6] = {
+    {48, 48, 64, 64, 1, 0},       {48, 48, 64, 64, 8, 0},       {96, 96, 128, 128, 1, 0},
+    {96, 96, 128, 128, 8, 0},     {192, 192, 256, 256, 1, 0},   {192, 192, 256, 256, 4, 0},
+    {384, 384, 512, 512, 1, 0},   {384, 384, 512, 512, 4, 0},   {384, 192, 512, 256, 1, 0},
+    {384, 192, 512, 256, 4, 0},   {192, 384, 256, 512, 1, 0},   {192, 384, 256, 512, 4, 0},
+    {48, 48, 64, 64, 1, 1},       {48, 48, 64, 64, 8, 1},       {96, 96, 128, 128, 1, 1},
+    {96, 96, 128, 128, 8, 1},     {192, 192, 256, 256, 1, 1},   {192, 192, 256, 256, 4, 1},
+    {384, 384, 512, 512, 1, 1},   {384, 384, 512, 512, 4, 1},   {384, 192, 512, 256, 1, 1},
+    {384, 192, 512, 256, 4, 1},   {192, 384, 256, 512, 1, 1},   {192, 384, 256, 512, 4, 1},
+    {16, 16, 64, 64, 1, 1},       {16, 16, 64, 64, 8, 1},       {32, 32, 128, 128, 1, 1},
+    {32, 32, 128, 128, 8, 1},     {64, 64, 256, 256, 1, 1},     {64, 64, 256, 256, 4, 1},
+    {128, 128, 512, 512, 1, 1},   {128, 128, 512, 512, 4, 1},   {128, 64, 512, 256, 1, 1},
+    {128, 64, 512, 256, 4, 1},    {64, 128, 256, 512, 1, 1},    {64, 128, 256, 512, 4, 1},
+    {512, 512, 4096, 4096, 1, 1}, {512, 512, 4096, 4096, 4, 1}, {512, 512, 4096, 4096, 8, 1},
+    {512, 512, 4096, 4096, 12, 1}, {512, 512, 4096, 4096, 16, 1}, {512, 512, 4096, 4096, 20, 1},
+    {512, 512, 4096, 4096, 24, 1}, {512, 512, 4096, 4096, 28, 1}, {512, 512, 4096, 4096, 32, 1},
+    // 2DTM workloads: 1024^2 / 128^2, 4096^2 / 256^2, 4096^2 / 512^2,
+    // 3840^2 / 384^2 (radix-3/5 path), 4096^2 / 384^2.
+    {128, 128, 1024, 1024, 4, 1}, {256, 256, 4096, 4096, 32, 1}, {512, 512, 4096, 4096, 64, 1},
+    {384, 384, 3840, 3840, 128, 1}, {384, 384, 4096, 4096, 256, 1},
+};
+
+int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes,
+        const void* conv_data, float* output, int oy, int ox, int H, int W, bool conj,
+        int device, void* stream) {
+    g_last_error.clear();
+    if (batch < 0) return fail(ZFFT_ERROR_INVALID_VALUE, "batch must be >= 0. Got %d.", batch);
+    if (sy < 1 || sx < 1)
+        return fail(ZFFT_ERROR_INVALID_VALUE, "signal lengths must be >= 1. Got (%d, %d).", sy, sx);
+    if (!supported(H) || !supported(W))
+        return fail(ZFFT_ERROR_UNSUPPORTED,
+                    "Unsupported padded convolution configuration: signal_y=%d, signal_x=%d, "
+                    "fft_y=%d, fft_x=%d, batch=%d, cross_correlate=%d (FFT sizes must be one of "
+                    "64..4096 powers of two or 120, 240, 480, 960, 1920, 3840)",
+                    sy, sx, H, W, batch, conj ? 1 : 0);
+    if (sy > H || sx > W)
+        return fail(ZFFT_ERROR_INVALID_VALUE,
+                    "signal (%d, %d) larger than the FFT size (%d, %d)", sy, sx, H, W);
+    const int vy = H - sy + 1, vx = W - sx + 1;
+    const bool valid_out = (oy == vy && ox == vx);
+    const bool full_out = (oy == H && ox == W);
+    if (!valid_out && !full_out) {
+        if (ox != vx && ox != W)
+            return fail(ZFFT_ERROR_INVALID_VALUE,
+                        "Output tensor last dimension must be fft_size_x - signal_length_x + 1 "
+                        "(%d) or fft_size_x (%d). Got %d.",
+                        vx, W, ox);
+        return fail(ZFFT_ERROR_INVALID_VALUE,
+                    "Output tensor second-to-last dimension must be fft_size_y - signal_length_y "
+                    "+ 1 (%d) or fft_size_y (%d) matching the last dimension. Got %d.",
+                    vy, H, oy);
+    }
+    const size_t need = zfft_workspace_bytes(H, W);
+    if (ws_bytes < need)
+        return fail(ZFFT_ERROR_INVALID_VALUE, "FFT workspace too small: %zu bytes, need %zu.",
+                    ws_bytes, need);
+    if (batch == 0) return ZFFT_SUCCESS;
+    if (!input || !ws || !conv_data || !output)
+        return fail(ZFFT_ERROR_INVALID_VALUE, "null data pointer");
+    if (!aligned(input, 4) || !aligned(output, 4) || !aligned(ws, 8) || !aligned(conv_data, 8))
+        return fail(ZFFT_ERROR_INVALID_VALUE,
+                    "misaligned pointer: float32 buffers need 4-byte, complex64 8-byte alignment");
+    int ndev = 0;
+    cudaError_t e = cudaGetDeviceCount(&ndev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+    if (device < 0 || device >= ndev || device >= kMaxDevices)
+        return fail(ZFFT_ERROR_INVALID_VALUE, "invalid device index %d (%d devices)", device, ndev);
+
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess) return cuda_fail(guard.err, "cudaSetDevice");
+    int rc = ensure_device(device);
+    if (rc != ZFFT_SUCCESS) return rc;
+
+    const float2* pool = g_dev_pool[device];
+    const float2* twH = pool + tw_offset(H);
+    const float2* twW = pool + tw_offset(W);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float2* slice = static_cast<float2*>(ws);
+    const float2* spec = static_cast<const float2*>(conv_data);
+    const int W2 = W / 2;
+    const int nz_col = stage0_nz(H, sy);
+    const int nz_row = stage0_nz(W2, (sx + 1) / 2);
+    const float scale = float(1.0 / (double(H) * double(W)));
+    ColFn col = col_fn(H);
+    R2cFn r2c = r2c_fn(W);
+    C2rFn c2r = c2r_fn(W);
+
+    if (g_timer.on) g_timer.device = device;
+    for (int t = 0; t < batch; ++t) {
+        const float* tmpl = input + (size_t)t * sy * sx;
+        float* out = output + (size_t)t * oy * ox;
+        int m = timer_mark(s);
+        e = r2c(tmpl, slice, twW, sy, sx, H, scale, nz_row, device, s);
+        if (e != cudaSuccess) return cuda_fail(e, "row r2c launch");
+        timer_close(0, m, s);
+        m = timer_mark(s);
+        e = col(slice, spec, twH, sy, W2, oy, conj, nz_col, device, s);
+        if (e != cudaSuccess) return cuda_fail(e, "column launch");
+        timer_close(1, m, s);
+        m = timer_mark(s);
+        e = c2r(slice, out, twW, H, oy, ox, ox, device, s);
+        if (e != cudaSuccess) return cuda_fail(e, "row c2r launch");
+        timer_close(2, m, s);
+    }
+    return ZFFT_SUCCESS;
+}
+
+}  // namespace
+
+namespace zf {
+int plan_first_radix(int n) { return make_plan(n).R[0]; }
+}  // namespace zf
+
+extern "C" {
+
+int zfft_padded_real_corr_2d(const float* input, int batch, int signal_y, int signal_x,
+                             void* fft_workspace, size_t fft_workspace_bytes,
+                             const void* conv_data, float* output, int output_y, int output_x,
+                             int fft_size_y, int fft_size_x, int device, void* stream) {
+    return run(input, batch, signal_y, signal_x, fft_workspace, fft_workspace_bytes, conv_data,
+               output, output_y, output_x, fft_size_y, fft_size_x, true, device, stream);
+}
+
+int zfft_padded_real_conv_2d(const float* input, int batch, int signal_y, int signal_x,
+                             void* fft_workspace, size_t fft_workspace_bytes,
+                             const void* conv_data, float* output, int output_y, int output_x,
+                             int fft_size_y, int fft_size_x, int device, void* stream) {
+    return run(input, batch, signal_y, signal_x, fft_workspace, fft_workspace_bytes, conv_data,
+               output, output_y, output_x, fft_size_y, fft_size_x, false, device, stream);
+}
+
+size_t zfft_workspace_bytes(int fft_size_y, int fft_size_x) {
+    if (!supported(fft_size_y) || !supported(fft_size_x)) return 0;
+    return (size_t)fft_size_y * (size_t)(fft_size_x / 2) * sizeof(float2);
+}
+
+int zfft_is_fft_size_supported(int n) { return supported(n) ? 1 : 0; }
+
+int zfft_get_supported_conv_configs(int* records, int capacity) {
+    const int n = int(sizeof(kConfigs) / sizeof(kConfigs[0]));
+    for (int i = 0; i < n && i < capacity && records; ++i)
+        std::memcpy(records + 6 * i, kConfigs[i], sizeof(kConfigs[i]));
+    return n;
+}
+
+const char* zfft_get_last_error(void) { return g_last_error.c_str(); }
+
+int zfft_stage_timing_enable(int enable) {
+    g_timer.on = enable != 0;
+    return ZFFT_SUCCESS;
+}
+
+int zfft_stage_timing_read(double* ms, int* launches, int n) {
+    if (n < kStages || !ms || !launches)
+        return fail(ZFFT_ERROR_INVALID_VALUE, "stage timing needs arrays of %d entries", kStages);
+    for (int st = 0; st < kStages; ++st) {
+        ms[st] = 0.0;
+        launches[st] = 0;
+        for (auto& pr : g_timer.marks[st]) {
+            cudaError_t e = cudaEventSynchronize(g_timer.pool[pr.second]);
+            if (e != cudaSuccess) return cuda_fail(e, "stage timing event");
+            float f = 0.f;
+            e = cudaEventElapsedTime(&f, g_timer.pool[pr.first], g_timer.pool[pr.second]);
+            if (e != cudaSuccess) return cuda_fail(e, "stage timing elapsed");
+            ms[st] += f;
+            launches[st] += 1;
+        }
+        g_timer.marks[st].clear();
+    }
+    g_timer.used = 0;
+    return ZFFT_SUCCESS;
+}
+
+int zfft_get_version(void) { return kVersion; }
+
+}  // extern "C"

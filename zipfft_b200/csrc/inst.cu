@@ -1,0 +1,135 @@
+// Kernel instantiations and launchers for one FFT size.  Compiled once per
+// size with -DZF_SIZE=<n> (the build runs these compilations in parallel); each
+// object defines launch_col_<n>, launch_row_r2c_<n> and launch_row_c2r_<n>.
+//
+// Replaces the per-configuration template instantiation of zipFFT's launcher
+// (src/cuda/real_conv_2d.cuh:153-293 and the compile-time shape table in
+// src/cuda/real_conv_2d_binding.cu:51-140): shapes other than the FFT size are
+// run-time values here.
+#include <mutex>
+
+#include "launch.h"
+#include "xcorr_kernels.cuh"
+
+#ifndef ZF_SIZE
+#error "compile once per FFT size with -DZF_SIZE=<n>"
+#endif
+
+namespace zf {
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+// Per kernel instance and device: dynamic shared memory opt-in and the number
+// of co-resident blocks, computed once.
+struct KernelState {
+    std::once_flag once[kMaxDevices];
+    int grid_cap[kMaxDevices];
+    cudaError_t err[kMaxDevices];
+};
+
+template <class Kern>
+cudaError_t configure(Kern kernel, KernelState& st, int smem, int threads, int device, int* cap) {
+    if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
+    std::call_once(st.once[device], [&] {
+        cudaError_t e = cudaSuccess;
+        if (smem > 48 * 1024)
+            e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        int occ = 0, sms = 0;
+        if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, threads, smem);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+        st.err[device] = e;
+        st.grid_cap[device] = occ * sms;
+    });
+    *cap = st.grid_cap[device];
+    if (st.err[device] != cudaSuccess) return st.err[device];
+    return *cap > 0 ? cudaSuccess : cudaErrorInvalidConfiguration;
+}
+
+inline int min_int(int a, int b) { return a < b ? a : b; }
+
+template <int H, bool CONJ, int NZ>
+cudaError_t col_t(float2* ws, const float2* spec, const float2* tw, int h, int W2, int store_rows,
+                  int device, cudaStream_t s) {
+    using C = ColCfg<H>;
+    static KernelState st;
+    auto kernel = k_col_fused<H, CONJ, NZ>;
+    int cap = 0;
+    cudaError_t e = configure(kernel, st, C::SMEM, C::THREADS, device, &cap);
+    if (e != cudaSuccess) return e;
+    const int grid = min_int((W2 + 1 + C::FPB - 1) / C::FPB, cap);
+    kernel<<<grid, C::THREADS, C::SMEM, s>>>(ws, spec, tw, h, W2, store_rows);
+    return cudaGetLastError();
+}
+
+template <int W2, int NZ>
+cudaError_t r2c_t(const float* tmpl, float2* ws, const float2* tw, int h, int w, int H,
+                  float scale, int device, cudaStream_t s) {
+    using C = RowCfg<W2>;
+    static KernelState st;
+    auto kernel = k_row_r2c<W2, NZ>;
+    int cap = 0;
+    cudaError_t e = configure(kernel, st, C::SMEM, C::THREADS, device, &cap);
+    if (e != cudaSuccess) return e;
+    const int grid = min_int((h + C::RPB - 1) / C::RPB, cap);
+    kernel<<<grid, C::THREADS, C::SMEM, s>>>(tmpl, ws, tw, h, w, H, scale);
+    return cudaGetLastError();
+}
+
+template <int W2>
+cudaError_t c2r_t(const float2* ws, float* out, const float2* tw, int H, int out_rows,
+                  int out_cols, int out_pitch, int device, cudaStream_t s) {
+    using C = RowCfg<W2>;
+    static KernelState st;
+    auto kernel = k_row_c2r<W2>;
+    int cap = 0;
+    cudaError_t e = configure(kernel, st, C::SMEM, C::THREADS, device, &cap);
+    if (e != cudaSuccess) return e;
+    const int grid = min_int((out_rows + C::RPB - 1) / C::RPB, cap);
+    kernel<<<grid, C::THREADS, C::SMEM, s>>>(ws, out, tw, H, out_rows, out_cols, out_pitch);
+    return cudaGetLastError();
+}
+
+// The pruned starts (nz = 1, 2) are instantiated for sizes >= 1024, where
+// templates are much smaller than the image; smaller sizes use the full start.
+constexpr bool kPruned = ZF_SIZE >= 1024;
+
+}  // namespace
+
+#define ZF_CAT2(a, b) a##b
+#define ZF_CAT(a, b) ZF_CAT2(a, b)
+
+cudaError_t ZF_CAT(launch_col_, ZF_SIZE)(float2* ws, const float2* spec, const float2* tw, int h,
+                                         int W2, int store_rows, bool conj, int nz, int device,
+                                         cudaStream_t s) {
+    constexpr int H = ZF_SIZE;
+    if constexpr (kPruned) {
+        if (nz == 1)
+            return conj ? col_t<H, true, 1>(ws, spec, tw, h, W2, store_rows, device, s)
+                        : col_t<H, false, 1>(ws, spec, tw, h, W2, store_rows, device, s);
+        if (nz == 2)
+            return conj ? col_t<H, true, 2>(ws, spec, tw, h, W2, store_rows, device, s)
+                        : col_t<H, false, 2>(ws, spec, tw, h, W2, store_rows, device, s);
+    }
+    return conj ? col_t<H, true, 0>(ws, spec, tw, h, W2, store_rows, device, s)
+                : col_t<H, false, 0>(ws, spec, tw, h, W2, store_rows, device, s);
+}
+
+cudaError_t ZF_CAT(launch_row_r2c_, ZF_SIZE)(const float* tmpl, float2* ws, const float2* tw,
+                                             int h, int w, int H, float scale, int nz, int device,
+                                             cudaStream_t s) {
+    constexpr int W2 = ZF_SIZE / 2;
+    if constexpr (kPruned) {
+        if (nz == 1) return r2c_t<W2, 1>(tmpl, ws, tw, h, w, H, scale, device, s);
+        if (nz == 2) return r2c_t<W2, 2>(tmpl, ws, tw, h, w, H, scale, device, s);
+    }
+    return r2c_t<W2, 0>(tmpl, ws, tw, h, w, H, scale, device, s);
+}
+
+cudaError_t ZF_CAT(launch_row_c2r_, ZF_SIZE)(const float2* ws, float* out, const float2* tw, int H,
+                                             int out_rows, int out_cols, int out_pitch, int device,
+                                             cudaStream_t s) {
+    return c2r_t<ZF_SIZE / 2>(ws, out, tw, H, out_rows, out_cols, out_pitch, device, s);
+}
+
+}  // namespace zf

@@ -1,0 +1,155 @@
+"""zipfft.padded_rconv2d: padded real 2D convolution / cross-correlation.
+
+Drop-in for the reference's pybind11 module of the same name
+(mgiammar/zipFFT src/cuda/real_conv_2d_binding.cu:301-308): same functions,
+argument order and meaning, the same validation messages (binding.cu:196-263)
+raised as RuntimeError, and the same stream/device behaviour (launch on
+torch.cuda.current_stream of the input's device, no host synchronisation,
+binding.cu:192-194 and :266).
+
+Differences, all supersets of the reference:
+  * shapes are run-time values: any signal size up to the FFT size and any
+    batch, for the FFT sizes in `supported_fft_sizes()` (the reference only
+    accepts the 45 compiled shapes of binding.cu:51-106);
+  * `output` may also be the full circular map (..., H, W) instead of the
+    valid crop (..., H-h+1, W-w+1);
+  * tensors must be contiguous (the reference silently assumed it);
+  * CUDA failures raise instead of terminating the process.
+The computation runs only in libzipfft_b200.so (CUDA, sm_100a); there is no
+CPU path.
+"""
+from __future__ import annotations
+
+from typing import List, Tuple
+
+import torch
+
+from . import _lib
+
+__all__ = ["corr", "conv", "get_supported_conv_configs", "supported_fft_sizes",
+           "workspace_bytes"]
+
+
+def _check(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _validate(input: torch.Tensor, fft_workspace: torch.Tensor, conv_data: torch.Tensor,
+              output: torch.Tensor, fft_size_y: int, fft_size_x: int):
+    """Checks of real_conv_2d_binding.cu:196-263, same order and messages."""
+    _check(input.device.type == "cuda", "Input tensor must be on CUDA device")
+    _check(fft_workspace.device.type == "cuda", "FFT workspace tensor must be on CUDA device")
+    _check(conv_data.device.type == "cuda", "Convolution data tensor must be on CUDA device")
+    _check(output.device.type == "cuda", "Output tensor must be on CUDA device")
+    ref = input.device
+    _check(fft_workspace.device == ref,
+           "FFT workspace tensor must be on the same device as the input tensor")
+    _check(conv_data.device == ref,
+           "Convolution data tensor must be on the same device as the input tensor")
+    _check(output.device == ref, "Output tensor must be on the same device as the input tensor")
+    _check(input.dtype == torch.float32, "Input tensor must be of type torch.float32")
+    _check(fft_workspace.dtype == torch.complex64,
+           "FFT workspace tensor must be of type torch.complex64 (float2)")
+    _check(conv_data.dtype == torch.complex64,
+           "Convolution data tensor must be of type torch.complex64 (float2)")
+    _check(output.dtype == torch.float32, "Output tensor must be of type torch.float32")
+
+    if input.dim() == 2:
+        batch, sy, sx = 1, input.size(0), input.size(1)
+    elif input.dim() == 3:
+        batch, sy, sx = input.size(0), input.size(1), input.size(2)
+    else:
+        raise RuntimeError(f"Input tensor must be 2D or 3D. Got {input.dim()}D.")
+
+    stride = fft_size_x // 2 + 1
+    _check(fft_workspace.dim() == input.dim(),
+           "FFT workspace tensor must have the same number of dimensions as the input tensor")
+    _check(fft_workspace.size(-1) == stride,
+           "FFT workspace tensor last dimension must be fft_size_x/2 + 1")
+    _check(fft_workspace.size(-2) == fft_size_y,
+           "FFT workspace tensor second-to-last dimension must be fft_size_y")
+    if batch > 1:
+        _check(fft_workspace.size(0) == batch,
+               "FFT workspace tensor first dimension (batch) must match input batch size")
+
+    # The two messages below are the reference's text verbatim (binding.cu:252-255).
+    _check(conv_data.dim() == 2, f"Convolution data tensor must be 2D. Got {conv_data.dim()}D.")
+    _check(conv_data.size(0) == stride,
+           "Convolution data tensor first dimension must match fft_size_y")
+    _check(conv_data.size(1) == fft_size_y,
+           "Convolution data tensor second dimension must be fft_size_x/2 + 1")
+
+    vx, vy = fft_size_x - sx + 1, fft_size_y - sy + 1
+    _check(output.dim() == input.dim(),
+           "Output tensor must have the same number of dimensions as the input tensor")
+    full = output.size(-1) == fft_size_x and output.size(-2) == fft_size_y
+    if not full:
+        _check(output.size(-1) == vx,
+               "Output tensor last dimension must be fft_size_x - signal_length_x + 1")
+        _check(output.size(-2) == vy,
+               "Output tensor second-to-last dimension must be fft_size_y - signal_length_y + 1")
+    if output.dim() == 3:
+        _check(output.size(0) == batch, "Output tensor first dimension (batch) must match input "
+                                        "batch size")
+    for name, t in (("Input", input), ("FFT workspace", fft_workspace),
+                    ("Convolution data", conv_data), ("Output", output)):
+        _check(t.is_contiguous(), f"{name} tensor must be contiguous")
+    return batch, sy, sx, output.size(-2), output.size(-1)
+
+
+def _run(fn_name: str, input, fft_workspace, conv_data, output, fft_size_y: int,
+         fft_size_x: int) -> None:
+    batch, sy, sx, oy, ox = _validate(input, fft_workspace, conv_data, output, int(fft_size_y),
+                                      int(fft_size_x))
+    lib = _lib.load()
+    device = input.device.index if input.device.index is not None else torch.cuda.current_device()
+    stream = torch.cuda.current_stream(device).cuda_stream
+    ws_bytes = fft_workspace.numel() * fft_workspace.element_size()
+    status = getattr(lib, fn_name)(input.data_ptr(), batch, sy, sx, fft_workspace.data_ptr(),
+                                   ws_bytes, conv_data.data_ptr(), output.data_ptr(), oy, ox,
+                                   int(fft_size_y), int(fft_size_x), device, stream)
+    _lib.check(status)
+
+
+def corr(input: torch.Tensor, fft_workspace: torch.Tensor, conv_data: torch.Tensor,
+         output: torch.Tensor, fft_size_y: int, fft_size_x: int) -> None:
+    """2D padded real cross-correlation (binding.cu:295-299, :304).
+
+    input (h, w) or (B, h, w) float32; fft_workspace complex64 (H, W/2+1) or
+    (B, H, W/2+1), clobbered; conv_data complex64 (W/2+1, H) = rfftn(image).T;
+    output float32 (..., H-h+1, W-w+1) or (..., H, W), written in place."""
+    _run("zfft_padded_real_corr_2d", input, fft_workspace, conv_data, output, fft_size_y,
+         fft_size_x)
+
+
+def conv(input: torch.Tensor, fft_workspace: torch.Tensor, conv_data: torch.Tensor,
+         output: torch.Tensor, fft_size_y: int, fft_size_x: int) -> None:
+    """2D padded real convolution (binding.cu:288-292, :303); arguments as corr."""
+    _run("zfft_padded_real_conv_2d", input, fft_workspace, conv_data, output, fft_size_y,
+         fft_size_x)
+
+
+def get_supported_conv_configs() -> List[Tuple[int, int, int, int, int, bool]]:
+    """(signal_y, signal_x, fft_y, fft_x, batch, cross_correlate) tuples
+    (binding.cu:160-170): the reference's 45 shapes plus the 2DTM workloads.
+    Any other shape with supported FFT sizes runs as well."""
+    import ctypes
+
+    lib = _lib.load()
+    n = lib.zfft_get_supported_conv_configs(None, 0)
+    buf = (ctypes.c_int * (6 * n))()
+    lib.zfft_get_supported_conv_configs(buf, n)
+    return [(buf[6 * i], buf[6 * i + 1], buf[6 * i + 2], buf[6 * i + 3], buf[6 * i + 4],
+             bool(buf[6 * i + 5])) for i in range(n)]
+
+
+def supported_fft_sizes() -> List[int]:
+    """FFT sizes (for both H and W) compiled into the library."""
+    lib = _lib.load()
+    return [n for n in range(16, 8193) if lib.zfft_is_fft_size_supported(n)]
+
+
+def workspace_bytes(fft_size_y: int, fft_size_x: int) -> int:
+    """Workspace bytes the kernels use (one H x W/2 complex64 slice)."""
+    return int(_lib.load().zfft_workspace_bytes(int(fft_size_y), int(fft_size_x)))
