@@ -224,7 +224,7 @@ def run_reference_arm(args, world, rank):
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
-def cufft_torch_rate(spec_nat, tm_dev, steps=5, warmup=2):
+def cufft_torch_rate(spec_nat, tm_dev, steps=5, warmup=3):
     """The explicit-pad torch.fft (cuFFT) pipeline on the same GPU, for comparison."""
     import torch.nn.functional as F
 
@@ -244,13 +244,14 @@ def cufft_torch_rate(spec_nat, tm_dev, steps=5, warmup=2):
     torch.cuda.synchronize()
     del out
     ms = s.elapsed_time(e) / steps
-    return BATCH / (ms / 1e3), ms
+    return tm_dev.shape[0] / (ms / 1e3), ms
 
 
 def run_gpu_arm(args, world, rank, local):
     import zipfft
     from zipfft_b200 import _lib
 
+    BATCH = args.batch
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     stream = torch.cuda.current_stream(dev)
@@ -397,6 +398,9 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", choices=("zipfft", "reference"), default="zipfft")
     ap.add_argument("--skip-baselines", action="store_true",
                     help="skip the cuFFT comparison and the CPU baseline")
+    ap.add_argument("--batch", type=int, default=BATCH,
+                    help="templates per GPU per step (default 32, the benchmarked workload; "
+                         "smaller values only for profiling captures)")
     args = ap.parse_args(argv)
     args.warmup = max(args.warmup, 3)  # at least 3 untimed warm-up steps; reported as run
     if args.impl == "reference":

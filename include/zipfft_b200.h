@@ -42,11 +42,15 @@ extern "C" {
  * Replaces zipfft.padded_rconv2d.conv / .corr (real_conv_2d_binding.cu:288-299).
  *
  *   input         float32 [batch][signal_y][signal_x], contiguous
- *   fft_workspace complex64 scratch; at least zfft_workspace_bytes(fft_y, fft_x)
- *                 bytes (one (fft_y, fft_x/2 + 1) slice, as in the reference,
- *                 is always enough).  Clobbered.
- *   conv_data     complex64 [fft_x/2 + 1][fft_y]: rfft2 of the image, transposed
- *                 (the reference's pre-transposed layout, binding.cu:248-255)
+ *   fft_workspace complex64 scratch, 16-byte aligned; at least
+ *                 zfft_workspace_bytes(fft_y, fft_x) bytes (one
+ *                 (fft_y, fft_x/2 + 1) slice, as in the reference, is always
+ *                 enough; the reference's (batch, fft_y, fft_x/2 + 1) lets the
+ *                 row transforms of up to 16 templates run per launch).
+ *                 Clobbered.
+ *   conv_data     complex64 [fft_x/2 + 1][fft_y], 16-byte aligned: rfft2 of the
+ *                 image, transposed (the reference's pre-transposed layout,
+ *                 binding.cu:248-255)
  *   output        float32 [batch][output_y][output_x] where (output_y, output_x)
  *                 is either the valid crop (fft_y - signal_y + 1,
  *                 fft_x - signal_x + 1) as in the reference, or the full
@@ -95,6 +99,21 @@ ZFFT_API const char* zfft_get_last_error(void);
  * entries), then clears the record. */
 ZFFT_API int zfft_stage_timing_enable(int enable);
 ZFFT_API int zfft_stage_timing_read(double* ms, int* launches, int n);
+
+/* Device status: kernels never spin without bound.  Every wait on an
+ * asynchronous copy gives up after about a second; the kernel then records
+ * ZFFT_ERROR_TIMEOUT in a per-device status word and exits instead of hanging
+ * the GPU.  zfft_check_device_status synchronizes `stream`, stores the word
+ * (0 = no failure since the last check) in *status and clears it.  No
+ * counterpart in the reference, whose launcher only checks launch errors
+ * (real_conv_2d.cuh:279-289). */
+ZFFT_API int zfft_check_device_status(int device, void* stream, int* status);
+
+/* Runs a one-block kernel whose wait can never complete (its barrier expects
+ * more bytes than its copy delivers) with a ~1 ms limit, so that the timeout
+ * path can be exercised: afterwards zfft_check_device_status reports
+ * ZFFT_ERROR_TIMEOUT.  For tests. */
+ZFFT_API int zfft_selftest_wait_timeout(int device, void* stream);
 
 /* Library version as major * 10000 + minor * 100 + patch. */
 ZFFT_API int zfft_get_version(void);

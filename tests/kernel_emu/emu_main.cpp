@@ -9,11 +9,14 @@
 //
 // Usage: zf_emu <in.bin> <out.bin>
 //   in.bin : int32 header {B, sy, sx, H, W, oy, ox, conj, grid_cap, nz_col,
-//            nz_row}, float32 templates [B][sy][sx], complex64 spectrum
-//            [W/2+1][H]
+//            nz_row, chunk}, float32 templates [B][sy][sx], complex64
+//            spectrum [W/2+1][H]
 //   out.bin: float32 [B][oy][ox]
+#include <atomic>
 #include <barrier>
 #include <cmath>
+#include <map>
+#include <mutex>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -24,6 +27,9 @@
 struct float2 {
     float x, y;
 };
+struct __attribute__((aligned(16))) float4 {
+    float x, y, z, w;
+};
 struct dim3 {
     unsigned x = 1, y = 1, z = 1;
 };
@@ -32,11 +38,26 @@ struct dim3 {
 #define __host__
 #define __forceinline__ inline
 #define __launch_bounds__(...)
+#define __grid_constant__
 
 thread_local dim3 threadIdx, blockIdx, blockDim, gridDim;
 thread_local std::barrier<>* emu_barrier = nullptr;
 thread_local float2* emu_smem = nullptr;
+thread_local size_t emu_smem_bytes = 0;
+thread_local unsigned emu_or_calls = 0;
+std::atomic<int> emu_or_flags[2];
+
 inline void __syncthreads() { emu_barrier->arrive_and_wait(); }
+inline int __syncthreads_or(int pred) {
+    const unsigned slot = emu_or_calls++ & 1u;
+    if (pred) emu_or_flags[slot].store(1);
+    emu_barrier->arrive_and_wait();
+    const int r = emu_or_flags[slot].load();
+    emu_barrier->arrive_and_wait();
+    if (threadIdx.x == 0) emu_or_flags[slot].store(0);
+    return r;
+}
+inline int atomicExch(int* p, int v) { return __atomic_exchange_n(p, v, __ATOMIC_SEQ_CST); }
 template <class T>
 inline T __ldg(const T* p) {
     return *p;
@@ -46,22 +67,77 @@ inline T __ldg(const T* p) {
 
 float2* zf::dyn_smem() { return emu_smem; }
 
+// mbarrier stand-in: phase parity, pending arrivals, transaction bytes.
+struct EmuBar {
+    uint32_t phase = 0, count = 0, pending = 0;
+    long long tx = 0;
+};
+static std::mutex emu_bar_mu;
+static std::map<uint64_t*, EmuBar> emu_bars;
+static void emu_bar_complete(EmuBar& b) {
+    if (b.pending == 0 && b.tx == 0) {
+        b.phase ^= 1u;
+        b.pending = b.count;
+    }
+}
+void zf::emu_mbar_init(uint64_t* bar, uint32_t count) {
+    std::lock_guard<std::mutex> l(emu_bar_mu);
+    EmuBar b;
+    b.count = b.pending = count;
+    emu_bars[bar] = b;
+}
+void zf::emu_mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    std::lock_guard<std::mutex> l(emu_bar_mu);
+    EmuBar& b = emu_bars.at(bar);
+    b.tx += bytes;
+    if (b.pending == 0) std::abort();
+    b.pending -= 1;
+    emu_bar_complete(b);
+}
+void zf::emu_mbar_complete_tx(uint64_t* bar, uint32_t bytes) {
+    std::lock_guard<std::mutex> l(emu_bar_mu);
+    EmuBar& b = emu_bars.at(bar);
+    b.tx -= bytes;
+    emu_bar_complete(b);
+}
+bool zf::emu_mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    std::lock_guard<std::mutex> l(emu_bar_mu);
+    return emu_bars.at(bar).phase != parity;  // the phase with that parity completed
+}
+// TMA rules: 16-byte aligned addresses and sizes, destination inside the
+// block's shared memory.
+void zf::emu_check_copy(const void* dst, const void* src, uint32_t bytes) {
+    const auto d = reinterpret_cast<uintptr_t>(dst), s = reinterpret_cast<uintptr_t>(src);
+    const auto lo = reinterpret_cast<uintptr_t>(emu_smem);
+    if (d % 16 || s % 16 || bytes % 16 || d < lo || d + bytes > lo + emu_smem_bytes) {
+        std::fprintf(stderr, "bad TMA copy dst=%p src=%p bytes=%u\n", dst, src, bytes);
+        std::abort();
+    }
+}
+
 template <class K, class... A>
-void emu_launch(int grid, int block, size_t smem_bytes, K kernel, A... args) {
-    std::vector<float2> smem((smem_bytes + 7) / 8);
+void emu_launch(dim3 grid, int block, size_t smem_bytes, K kernel, A... args) {
+    // 128-byte aligned like the device's dynamic shared memory.
+    std::vector<float4> store((smem_bytes + 15) / 16 + 8);
+    float2* smem = reinterpret_cast<float2*>((reinterpret_cast<uintptr_t>(store.data()) + 127) & ~uintptr_t(127));
     std::barrier<> bar(block);
     std::vector<std::thread> threads;
     for (int tid = 0; tid < block; ++tid) {
         threads.emplace_back([&, tid] {
             threadIdx.x = tid;
             blockDim.x = block;
-            gridDim.x = grid;
+            gridDim = grid;
             emu_barrier = &bar;
-            emu_smem = smem.data();
-            for (int b = 0; b < grid; ++b) {
-                blockIdx.x = b;
-                kernel(args...);
-                bar.arrive_and_wait();
+            emu_smem = smem;
+            emu_smem_bytes = smem_bytes;
+            emu_or_calls = 0;
+            for (unsigned by = 0; by < grid.y; ++by) {
+                for (unsigned bx = 0; bx < grid.x; ++bx) {
+                    blockIdx.x = bx;
+                    blockIdx.y = by;
+                    kernel(args...);
+                    bar.arrive_and_wait();
+                }
             }
         });
     }
@@ -77,65 +153,74 @@ static std::vector<float2> twiddles(int n) {
     return t;
 }
 
+static int g_status = 0;
+
 template <int H, bool CONJ, int NZ>
-void run_col(float2* ws, const float2* spec, const float2* tw, int h, int W2, int rows, int cap) {
-    using C = zf::ColCfg<H>;
+void run_col(float2* Q, const float2* R, int r_pitch, const float2* spec, const float2* tw, int h,
+             int W2, int rows, int cap) {
+    using C = zf::ColCfg<H, NZ>;
     int grid = (W2 + 1 + C::FPB - 1) / C::FPB;
     if (grid > cap) grid = cap;
-    emu_launch(grid, C::THREADS, C::SMEM, zf::k_col_fused<H, CONJ, NZ>, ws, spec, tw, h, W2, rows);
+    emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_col_fused<H, CONJ, NZ>, Q, R,
+               r_pitch, spec, tw, h, W2, rows, &g_status);
 }
 template <int W2, int NZ>
-void run_r2c(const float* tm, float2* ws, const float2* tw, int h, int w, int H, float sc, int cap) {
-    using C = zf::RowCfg<W2>;
-    int grid = (h + C::RPB - 1) / C::RPB;
-    if (grid > cap) grid = cap;
-    emu_launch(grid, C::THREADS, C::SMEM, zf::k_row_r2c<W2, NZ>, tm, ws, tw, h, w, H, sc);
+void run_r2c(const float* tm, float2* R, const float2* tw, int h, int w, int r_pitch,
+             long long r_tstride, int nt, float sc, int cap) {
+    using C = zf::R2cCfg<W2>;
+    int groups = (h + C::RPB - 1) / C::RPB;
+    int per = groups < cap ? groups : cap;
+    emu_launch(dim3{(unsigned)per, (unsigned)nt, 1}, C::THREADS, C::SMEM, zf::k_row_r2c<W2, NZ>, tm,
+               R, tw, h, w, r_pitch, r_tstride, sc);
 }
 template <int W2>
-void run_c2r(const float2* ws, float* out, const float2* tw, int H, int orows, int ocols, int cap) {
-    using C = zf::RowCfg<W2>;
-    int grid = (orows + C::RPB - 1) / C::RPB;
-    if (grid > cap) grid = cap;
-    emu_launch(grid, C::THREADS, C::SMEM, zf::k_row_c2r<W2>, ws, out, tw, H, orows, ocols, ocols);
+void run_c2r(const float2* Q, int H, float* out, const float2* tw, int orows, int ocols, int cap) {
+    using C = zf::C2rCfg<W2>;
+    zf::CUtensorMap map{reinterpret_cast<const unsigned char*>(Q), H, W2, (long long)H * 8,
+                        C::RPB, C::BOXK, 8};
+    int groups = (orows + C::RPB - 1) / C::RPB;
+    int grid = groups < cap ? groups : cap;
+    emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_row_c2r<W2>, map, out, tw,
+               orows, ocols, ocols, &g_status);
 }
 
 #define EMU_SIZES(X) X(64) X(128) X(256) X(120) X(240)
 
-static void col(int H, bool conj, int nz, float2* ws, const float2* spec, const float2* tw, int h,
-                int W2, int rows, int cap) {
-#define X(N)                                                                                 \
-    if (H == N) {                                                                            \
-        if (conj) {                                                                          \
-            if (nz == 1) return run_col<N, true, 1>(ws, spec, tw, h, W2, rows, cap);        \
-            if (nz == 2) return run_col<N, true, 2>(ws, spec, tw, h, W2, rows, cap);        \
-            return run_col<N, true, 0>(ws, spec, tw, h, W2, rows, cap);                     \
-        }                                                                                    \
-        if (nz == 1) return run_col<N, false, 1>(ws, spec, tw, h, W2, rows, cap);           \
-        if (nz == 2) return run_col<N, false, 2>(ws, spec, tw, h, W2, rows, cap);           \
-        return run_col<N, false, 0>(ws, spec, tw, h, W2, rows, cap);                        \
+static void col(int H, bool conj, int nz, float2* Q, const float2* R, int rp, const float2* spec,
+                const float2* tw, int h, int W2, int rows, int cap) {
+#define X(N)                                                                                   \
+    if (H == N) {                                                                              \
+        if (conj) {                                                                            \
+            if (nz == 1) return run_col<N, true, 1>(Q, R, rp, spec, tw, h, W2, rows, cap);     \
+            if (nz == 2) return run_col<N, true, 2>(Q, R, rp, spec, tw, h, W2, rows, cap);     \
+            return run_col<N, true, 0>(Q, R, rp, spec, tw, h, W2, rows, cap);                  \
+        }                                                                                      \
+        if (nz == 1) return run_col<N, false, 1>(Q, R, rp, spec, tw, h, W2, rows, cap);        \
+        if (nz == 2) return run_col<N, false, 2>(Q, R, rp, spec, tw, h, W2, rows, cap);        \
+        return run_col<N, false, 0>(Q, R, rp, spec, tw, h, W2, rows, cap);                     \
     }
     EMU_SIZES(X)
 #undef X
     std::fprintf(stderr, "unsupported H %d\n", H);
     std::exit(2);
 }
-static void r2c(int W, int nz, const float* tm, float2* ws, const float2* tw, int h, int w, int H,
-                float sc, int cap) {
-#define X(N)                                                              \
-    if (W == N) {                                                         \
-        if (nz == 1) return run_r2c<N / 2, 1>(tm, ws, tw, h, w, H, sc, cap); \
-        if (nz == 2) return run_r2c<N / 2, 2>(tm, ws, tw, h, w, H, sc, cap); \
-        return run_r2c<N / 2, 0>(tm, ws, tw, h, w, H, sc, cap);              \
+static void r2c(int W, int nz, const float* tm, float2* R, const float2* tw, int h, int w, int rp,
+                long long rts, int nt, float sc, int cap) {
+#define X(N)                                                                           \
+    if (W == N) {                                                                      \
+        if (nz == 1) return run_r2c<N / 2, 1>(tm, R, tw, h, w, rp, rts, nt, sc, cap);  \
+        if (nz == 2) return run_r2c<N / 2, 2>(tm, R, tw, h, w, rp, rts, nt, sc, cap);  \
+        return run_r2c<N / 2, 0>(tm, R, tw, h, w, rp, rts, nt, sc, cap);               \
     }
     EMU_SIZES(X)
 #undef X
     std::fprintf(stderr, "unsupported W %d\n", W);
     std::exit(2);
 }
-static void c2r(int W, const float2* ws, float* out, const float2* tw, int H, int orows, int ocols,
+static void c2r(int W, const float2* Q, int H, float* out, const float2* tw, int orows, int ocols,
                 int cap) {
 #define X(N) \
-    if (W == N) return run_c2r<N / 2>(ws, out, tw, H, orows, ocols, cap);
+    if (W == N) return run_c2r<N / 2>(Q, H, out, tw, orows, ocols, cap);
     EMU_SIZES(X)
 #undef X
     std::fprintf(stderr, "unsupported W %d\n", W);
@@ -149,11 +234,11 @@ int main(int argc, char** argv) {
     }
     FILE* f = std::fopen(argv[1], "rb");
     if (!f) return 2;
-    int hd[11];
-    if (std::fread(hd, sizeof(int), 11, f) != 11) return 2;
+    int hd[12];
+    if (std::fread(hd, sizeof(int), 12, f) != 12) return 2;
     const int B = hd[0], sy = hd[1], sx = hd[2], H = hd[3], W = hd[4], oy = hd[5], ox = hd[6];
     const bool conj = hd[7] != 0;
-    const int cap = hd[8], nz_col = hd[9], nz_row = hd[10];
+    const int cap = hd[8], nz_col = hd[9], nz_row = hd[10], chunk = hd[11];
     const int W2 = W / 2;
     std::vector<float> tm((size_t)B * sy * sx);
     std::vector<float2> spec((size_t)(W2 + 1) * H);
@@ -161,15 +246,40 @@ int main(int argc, char** argv) {
     if (std::fread(spec.data(), sizeof(float2), spec.size(), f) != spec.size()) return 2;
     std::fclose(f);
 
-    // Exactly the workspace the library asks for: H * W/2 complex values.
-    std::vector<float2> ws((size_t)H * W2);
+    // The host orchestration of zfft_padded_real_{corr,conv}_2d: Q (H x W2)
+    // first; with chunk > 0 the rows of `chunk` templates go to a region
+    // after Q with pitch round_up(h, 2), else into rows [0, h) of Q.
+    const long long h_pad = (sy + 1) / 2 * 2;
+    const long long q_elems = (long long)H * W2, r_elems = (long long)W2 * h_pad;
+    std::vector<float4> ws_store((q_elems + (chunk > 0 ? chunk : 0) * r_elems + 1) / 2 + 1);
+    float2* Q = reinterpret_cast<float2*>(ws_store.data());
+    float2* Rregion = Q + q_elems;
     std::vector<float> out((size_t)B * oy * ox);
     auto twH = twiddles(H), twW = twiddles(W);
     const float scale = float(1.0 / (double(H) * double(W)));
-    for (int t = 0; t < B; ++t) {
-        r2c(W, nz_row, tm.data() + (size_t)t * sy * sx, ws.data(), twW.data(), sy, sx, H, scale, cap);
-        col(H, conj, nz_col, ws.data(), spec.data(), twH.data(), sy, W2, oy, cap);
-        c2r(W, ws.data(), out.data() + (size_t)t * oy * ox, twW.data(), H, oy, ox, cap);
+    const int step = chunk > 0 ? chunk : 1;
+    for (int t0 = 0; t0 < B; t0 += step) {
+        const int n = B - t0 < step ? B - t0 : step;
+        if (chunk > 0)
+            r2c(W, nz_row, tm.data() + (size_t)t0 * sy * sx, Rregion, twW.data(), sy, sx, (int)h_pad,
+                r_elems, n, scale, cap);
+        for (int j = 0; j < n; ++j) {
+            const int t = t0 + j;
+            const float2* Rt = Q;
+            int rp = H;
+            if (chunk > 0) {
+                Rt = Rregion + (size_t)j * r_elems;
+                rp = (int)h_pad;
+            } else {
+                r2c(W, nz_row, tm.data() + (size_t)t * sy * sx, Q, twW.data(), sy, sx, H, 0, 1, scale, cap);
+            }
+            col(H, conj, nz_col, Q, Rt, rp, spec.data(), twH.data(), sy, W2, oy, cap);
+            c2r(W, Q, H, out.data() + (size_t)t * oy * ox, twW.data(), oy, ox, cap);
+        }
+    }
+    if (g_status != 0) {
+        std::fprintf(stderr, "device status %d\n", g_status);
+        return 3;
     }
     FILE* g = std::fopen(argv[2], "wb");
     if (!g) return 2;

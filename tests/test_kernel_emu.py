@@ -19,7 +19,7 @@ EXE = os.path.join(ROOT, "_build", "zf_emu")
 
 def _deps():
     files = [SRC] + [os.path.join(ROOT, "zipfft_b200", "csrc", f)
-                     for f in ("fft_core.cuh", "xcorr_kernels.cuh")]
+                     for f in ("fft_core.cuh", "xcorr_kernels.cuh", "async_copy.cuh")]
     return max(os.path.getmtime(f) for f in files)
 
 
@@ -45,7 +45,8 @@ def nz_of(n, length):
     return max(nz, 1) if nz <= 2 else 0
 
 
-def run_emu(exe, tmp_path, B, sy, sx, H, W, conj, full, nz_col=None, nz_row=None, seed=0):
+def run_emu(exe, tmp_path, B, sy, sx, H, W, conj, full, nz_col=None, nz_row=None, seed=0,
+            chunk=0):
     rng = np.random.default_rng(seed)
     img = rng.standard_normal((H, W)).astype(np.float32)
     tm = rng.standard_normal((B, sy, sx)).astype(np.float32)
@@ -55,7 +56,8 @@ def run_emu(exe, tmp_path, B, sy, sx, H, W, conj, full, nz_col=None, nz_row=None
     nz_row = nz_of(W // 2, (sx + 1) // 2) if nz_row is None else nz_row
     fin, fout = str(tmp_path / "in.bin"), str(tmp_path / "out.bin")
     with open(fin, "wb") as f:
-        np.array([B, sy, sx, H, W, oy, ox, int(conj), 3, nz_col, nz_row], np.int32).tofile(f)
+        np.array([B, sy, sx, H, W, oy, ox, int(conj), 3, nz_col, nz_row, chunk],
+                 np.int32).tofile(f)
         tm.tofile(f)
         spec.tofile(f)
     res = subprocess.run([exe, fin, fout], capture_output=True, text=True)
@@ -65,25 +67,28 @@ def run_emu(exe, tmp_path, B, sy, sx, H, W, conj, full, nz_col=None, nz_row=None
 
 
 CASES = [
-    # B, sy, sx, H, W, conj, full, nz_col, nz_row
-    (2, 16, 16, 64, 64, True, False, None, None),
-    (1, 48, 48, 64, 64, False, False, None, None),
-    (2, 12, 20, 64, 128, True, True, None, None),
-    (2, 5, 7, 120, 240, True, False, None, None),
-    (1, 32, 24, 128, 64, False, True, None, None),
-    (1, 16, 16, 256, 256, True, True, 1, 1),
-    (1, 30, 30, 256, 256, True, False, 2, 2),
-    (1, 17, 32, 256, 256, False, True, 2, 2),
-    (1, 100, 90, 240, 120, True, True, None, None),
-    (2, 64, 64, 64, 64, True, True, None, None),  # signal == FFT size
-    (1, 1, 1, 64, 64, True, True, 1, 1),          # single pixel
-    (1, 7, 3, 128, 240, True, False, 1, 1),       # odd widths
+    # B, sy, sx, H, W, conj, full, nz_col, nz_row, chunk
+    (2, 16, 16, 64, 64, True, False, None, None, 0),
+    (1, 48, 48, 64, 64, False, False, None, None, 0),
+    (2, 12, 20, 64, 128, True, True, None, None, 0),
+    (2, 5, 7, 120, 240, True, False, None, None, 0),
+    (1, 32, 24, 128, 64, False, True, None, None, 0),
+    (1, 16, 16, 256, 256, True, True, 1, 1, 0),
+    (1, 30, 30, 256, 256, True, False, 2, 2, 0),
+    (1, 17, 32, 256, 256, False, True, 2, 2, 0),
+    (1, 100, 90, 240, 120, True, True, None, None, 0),
+    (2, 64, 64, 64, 64, True, True, None, None, 0),  # signal == FFT size
+    (1, 1, 1, 64, 64, True, True, 1, 1, 0),          # single pixel
+    (1, 7, 3, 128, 240, True, False, 1, 1, 0),       # odd widths
+    (5, 16, 16, 64, 64, True, True, None, None, 2),  # chunked rows, partial last chunk
+    (3, 9, 13, 128, 256, False, False, None, None, 3),  # chunked, odd template
+    (4, 30, 30, 256, 256, True, True, 2, 2, 4),
 ]
 
 
 @pytest.mark.parametrize("case", CASES, ids=[str(c[:7]) for c in CASES])
 def test_emulated_kernels_match_oracle(emu, tmp_path, case):
-    B, sy, sx, H, W, conj, full, nzc, nzr = case
-    out, ref = run_emu(emu, tmp_path, B, sy, sx, H, W, conj, full, nzc, nzr)
+    B, sy, sx, H, W, conj, full, nzc, nzr, chunk = case
+    out, ref = run_emu(emu, tmp_path, B, sy, sx, H, W, conj, full, nzc, nzr, chunk=chunk)
     assert O.rel_l2(ref, out) < 1e-6
     assert O.max_abs_over_peak(ref, out) < 1e-5

@@ -155,3 +155,46 @@ def test_invalid_device_index_reports_error():
                                       cd.data_ptr(), out.data_ptr(), 64, 64, 64, 64, n + 3, None)
     assert st == _lib.ZFFT_ERROR_INVALID_VALUE
     assert "invalid device index" in _lib.last_error()
+
+
+@pytest.fixture(autouse=True)
+def _device_status_clean():
+    """No kernel may have given up on a bounded wait during any test."""
+    from zipfft_b200 import _lib
+
+    yield
+    assert _lib.check_device_status(0) == 0
+
+
+def test_bounded_wait_reports_timeout_and_context_survives():
+    """A wait that can never complete gives up (~1 ms limit) and reports
+    ZFFT_ERROR_TIMEOUT; the CUDA context stays usable afterwards."""
+    from zipfft_b200 import _lib
+
+    lib = _lib.load()
+    assert _lib.check_device_status(0) == 0
+    _lib.check(lib.zfft_selftest_wait_timeout(0, None))
+    assert _lib.check_device_status(0) == _lib.ZFFT_ERROR_TIMEOUT
+    assert _lib.check_device_status(0) == 0  # cleared by the read
+    _, tm, spec = make_inputs(2, 16, 16, 64, 64, seed=1)
+    out = capi_corr(tm, spec, 64, 64, True)
+    ref = O.padded_corr2d_f64(tm.numpy(), spec.numpy(), 64, 64, True, True)
+    assert_parity(ref, out, what="after timeout self-test")
+
+
+@pytest.mark.parametrize("H,h,B", [(4096, 256, 5), (1024, 100, 7), (3840, 384, 3)])
+def test_chunked_and_in_place_layouts_agree(H, h, B):
+    """Workspaces large enough for several templates' rows (chunked row
+    launches) give bit-identical results to the minimal in-place workspace."""
+    from zipfft_b200 import _lib
+
+    _, tm, spec = make_inputs(B, h, h, H, H, seed=H + B)
+    dev = torch.device("cuda", 0)
+    nmin = _lib.load().zfft_workspace_bytes(H, H) // 8
+    small = torch.empty(nmin, dtype=torch.complex64, device=dev)
+    big = torch.empty(B * H * (H // 2 + 1), dtype=torch.complex64, device=dev)
+    a = capi_corr(tm, spec, H, H, True, ws=small)
+    b = capi_corr(tm, spec, H, H, True, ws=big)
+    assert np.array_equal(a, b)
+    ref = O.padded_corr2d_f64(tm[B - 1].numpy(), spec.numpy(), H, H, True, True)
+    assert_parity(ref, a[B - 1], what="chunked layout, last template")

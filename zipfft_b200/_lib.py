@@ -31,6 +31,8 @@ SIGNATURES = {
     "zfft_get_supported_conv_configs": (_c_int, [ctypes.POINTER(ctypes.c_int), _c_int]),
     "zfft_get_last_error": (ctypes.c_char_p, []),
     "zfft_get_version": (_c_int, []),
+    "zfft_check_device_status": (_c_int, [_c_int, _vp, ctypes.POINTER(ctypes.c_int)]),
+    "zfft_selftest_wait_timeout": (_c_int, [_c_int, _vp]),
     "zfft_stage_timing_enable": (_c_int, [_c_int]),
     "zfft_stage_timing_read": (_c_int, [ctypes.POINTER(ctypes.c_double),
                                         ctypes.POINTER(ctypes.c_int), _c_int]),
@@ -98,3 +100,11 @@ def check(status: int) -> None:
     """Raise RuntimeError carrying the library's message for a non-zero status."""
     if status != ZFFT_SUCCESS:
         raise RuntimeError(last_error() or f"zipfft_b200 call failed with status {status}")
+
+
+def check_device_status(device: int, stream=None) -> int:
+    """Synchronize `stream` on `device` and return (and clear) the device
+    status word: 0, or ZFFT_ERROR_TIMEOUT if a kernel gave up on a wait."""
+    st = ctypes.c_int(0)
+    check(load().zfft_check_device_status(int(device), stream, ctypes.byref(st)))
+    return st.value

@@ -1,0 +1,153 @@
+// Asynchronous global -> shared copies on sm_100a: TMA bulk (1D) and tensor
+// (2D tile) loads completing on shared-memory mbarriers, and a bounded wait.
+//
+// No multicast form is used anywhere: every load fetches this GPU's own
+// memory into the issuing block's shared memory.
+//
+// Every wait is bounded: after kWaitLimitCycles of polling the waiter gives
+// up and the kernel reports ZFFT_ERROR_TIMEOUT through the device status word
+// instead of hanging.
+//
+// Host compilation (the CPU test harness of the kernel logic) provides
+// synchronous stand-ins with the same completion semantics.
+#pragma once
+
+#include <stdint.h>
+
+#include "fft_core.cuh"
+
+#if defined(__CUDACC__)
+#include <cuda.h>  // CUtensorMap
+#else
+#include <chrono>
+#include <cstring>
+#endif
+
+namespace zf {
+
+// Device status codes written by kernels (same values as the C ABI's).
+constexpr int kStatusTimeout = 4;
+// ~1 s at 2 GHz: far beyond any legitimate copy latency.
+constexpr long long kWaitLimitCycles = 2000000000LL;
+
+#if defined(__CUDACC__)
+
+ZF_DEV uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+ZF_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+
+// Make barrier initialisation visible to the async (TMA) proxy.
+ZF_DEV void mbar_init_fence() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+ZF_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+ZF_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// 1D bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned).
+ZF_DEV void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// 2D tile load of the tensor map's box at (x, y); x * element size must be a
+// multiple of 16 bytes.
+ZF_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+ZF_DEV long long cycle_clock() { return clock64(); }
+
+#else  // host stand-ins for the CPU test harness -------------------------------
+
+struct CUtensorMap {  // what the harness needs of a 2D tiled tensor map
+    const unsigned char* base;
+    long long dim0, dim1;  // elements
+    long long stride1;     // bytes between dim-1 rows
+    int box0, box1;
+    int elem;  // bytes per element
+};
+
+// Barrier word: low 32 bits phase, high 32 bits outstanding bytes + arrivals.
+void emu_mbar_init(uint64_t* bar, uint32_t count);
+void emu_mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes);
+void emu_mbar_complete_tx(uint64_t* bar, uint32_t bytes);
+bool emu_mbar_try_wait(uint64_t* bar, uint32_t parity);
+
+inline void mbar_init(uint64_t* bar, uint32_t count) { emu_mbar_init(bar, count); }
+inline void mbar_init_fence() {}
+inline void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    emu_mbar_arrive_expect_tx(bar, bytes);
+}
+inline bool mbar_try_wait(uint64_t* bar, uint32_t parity) { return emu_mbar_try_wait(bar, parity); }
+void emu_check_copy(const void* dst, const void* src, uint32_t bytes);
+inline void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    emu_check_copy(dst, src, bytes);
+    std::memcpy(dst, src, bytes);
+    emu_mbar_complete_tx(bar, bytes);
+}
+inline void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    unsigned char* d = static_cast<unsigned char*>(dst);
+    const int row = map->box0 * map->elem;
+    for (int j = 0; j < map->box1; ++j) {
+        const long long yy = (long long)y + j;
+        for (int i = 0; i < map->box0; ++i) {
+            const long long xx = (long long)x + i;
+            unsigned char* out = d + (size_t)j * row + (size_t)i * map->elem;
+            if (xx < 0 || yy < 0 || xx >= map->dim0 || yy >= map->dim1) {
+                std::memset(out, 0, map->elem);  // out-of-bounds fill
+            } else {
+                std::memcpy(out, map->base + yy * map->stride1 + xx * map->elem, map->elem);
+            }
+        }
+    }
+    emu_mbar_complete_tx(bar, (uint32_t)(map->box0 * map->box1 * map->elem));
+}
+inline long long cycle_clock() {  // nanoseconds stand in for cycles
+    return (long long)std::chrono::duration_cast<std::chrono::nanoseconds>(
+               std::chrono::steady_clock::now().time_since_epoch())
+        .count();
+}
+
+#endif
+
+// Bounded wait for the barrier phase with the given parity.
+ZF_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
+                              long long limit = kWaitLimitCycles) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = cycle_clock();
+    while (!mbar_try_wait(bar, parity)) {
+        if (cycle_clock() - t0 > limit) return false;
+    }
+    return true;
+}
+
+}  // namespace zf

@@ -17,14 +17,18 @@
 #include <string>
 #include <vector>
 
+#include <cudaTypedefs.h>
+
 #include "../../include/zipfft_b200.h"
+#include "async_copy.cuh"
 #include "fft_core.cuh"
 #include "launch.h"
 
 namespace {
 
-constexpr int kVersion = 100;  // 0.1.0
+constexpr int kVersion = 200;  // 0.2.0
 constexpr int kMaxDevices = 64;
+constexpr int kMaxChunk = 16;  // templates per row-r2c launch
 
 thread_local std::string g_last_error;
 
@@ -46,7 +50,13 @@ int cuda_fail(cudaError_t e, const char* what) {
 // Twiddle tables: w_N[m] = exp(-2 pi i m / N), one table per supported size,
 // computed in double precision on the host and uploaded once per device.
 // ---------------------------------------------------------------------------
-__device__ float2 g_tw_pool[ZF_TW_POOL_TOTAL];
+__device__ __align__(16) float2 g_tw_pool[ZF_TW_POOL_TOTAL];
+
+// Device status word: kernels that give up on a bounded wait write a
+// ZFFT_ERROR_* code here; zfft_check_device_status reads and clears it.
+__device__ int g_status;
+// 16-byte source of the bounded-wait self-test copy.
+__device__ __align__(16) float4 g_selftest_src;
 
 int tw_offset(int n) {
     int off = 0;
@@ -61,6 +71,7 @@ int tw_offset(int n) {
 std::mutex g_init_mu;
 bool g_dev_ready[kMaxDevices];
 float2* g_dev_pool[kMaxDevices];
+int* g_dev_status[kMaxDevices];
 
 int ensure_device(int device) {
     std::lock_guard<std::mutex> lock(g_init_mu);
@@ -83,6 +94,9 @@ int ensure_device(int device) {
     e = cudaGetSymbolAddress(&p, g_tw_pool);
     if (e != cudaSuccess) return cuda_fail(e, "resolving twiddle table address");
     g_dev_pool[device] = static_cast<float2*>(p);
+    e = cudaGetSymbolAddress(&p, g_status);
+    if (e != cudaSuccess) return cuda_fail(e, "resolving device status address");
+    g_dev_status[device] = static_cast<int*>(p);
     g_dev_ready[device] = true;
     return ZFFT_SUCCESS;
 }
@@ -141,11 +155,12 @@ void timer_close(int stage, int start, cudaStream_t s) {
     if (stop >= 0) g_timer.marks[stage].push_back({start, stop});
 }
 
-using ColFn = cudaError_t (*)(float2*, const float2*, const float2*, int, int, int, bool, int, int,
-                              cudaStream_t);
-using R2cFn = cudaError_t (*)(const float*, float2*, const float2*, int, int, int, float, int, int,
-                              cudaStream_t);
-using C2rFn = cudaError_t (*)(const float2*, float*, const float2*, int, int, int, int, int,
+using ColFn = cudaError_t (*)(float2*, const float2*, int, const float2*, const float2*, int, int,
+                              int, bool, int, int*, int, cudaStream_t);
+using R2cFn = cudaError_t (*)(const float*, float2*, const float2*, int, int, int, long long, int,
+                              float, int, int, cudaStream_t);
+using QmapFn = cudaError_t (*)(const float2*, int, CUtensorMap*);
+using C2rFn = cudaError_t (*)(const CUtensorMap*, float*, const float2*, int, int, int, int*, int,
                               cudaStream_t);
 
 ColFn col_fn(int n) {
@@ -158,6 +173,13 @@ ColFn col_fn(int n) {
 R2cFn r2c_fn(int n) {
 #define ZF_X(N) \
     if (n == (N)) return zf::launch_row_r2c_##N;
+    ZF_FOR_EACH_FFT_SIZE(ZF_X)
+#undef ZF_X
+    return nullptr;
+}
+QmapFn qmap_fn(int n) {
+#define ZF_X(N) \
+    if (n == (N)) return zf::make_qmap_##N;
     ZF_FOR_EACH_FFT_SIZE(ZF_X)
 #undef ZF_X
     return nullptr;
@@ -241,9 +263,10 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
     if (batch == 0) return ZFFT_SUCCESS;
     if (!input || !ws || !conv_data || !output)
         return fail(ZFFT_ERROR_INVALID_VALUE, "null data pointer");
-    if (!aligned(input, 4) || !aligned(output, 4) || !aligned(ws, 8) || !aligned(conv_data, 8))
+    if (!aligned(input, 4) || !aligned(output, 4) || !aligned(ws, 16) || !aligned(conv_data, 16))
         return fail(ZFFT_ERROR_INVALID_VALUE,
-                    "misaligned pointer: float32 buffers need 4-byte, complex64 8-byte alignment");
+                    "misaligned pointer: input/output need 4-byte alignment, fft_workspace and "
+                    "conv_data 16-byte alignment (TMA copies)");
     int ndev = 0;
     cudaError_t e = cudaGetDeviceCount(&ndev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
@@ -256,35 +279,74 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
     if (rc != ZFFT_SUCCESS) return rc;
 
     const float2* pool = g_dev_pool[device];
+    int* status = g_dev_status[device];
     const float2* twH = pool + tw_offset(H);
     const float2* twW = pool + tw_offset(W);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    float2* slice = static_cast<float2*>(ws);
+    float2* Q = static_cast<float2*>(ws);
     const float2* spec = static_cast<const float2*>(conv_data);
     const int W2 = W / 2;
     const int nz_col = stage0_nz(H, sy);
     const int nz_row = stage0_nz(W2, (sx + 1) / 2);
     const float scale = float(1.0 / (double(H) * double(W)));
+
+    // Workspace layout: Q (H x W2) first.  If the workspace holds more, the
+    // row transforms of up to kMaxChunk templates run in one launch into a
+    // region after Q (pitch h_pad); otherwise each template's rows go into
+    // rows [0, h) of Q itself (pitch H).
+    const long long h_pad = (sy + 1) / 2 * 2;
+    const long long q_elems = (long long)H * W2;
+    const long long r_elems = (long long)W2 * h_pad;
+    const long long avail = (long long)(ws_bytes / sizeof(float2)) - q_elems;
+    int chunk = 0;
+    if (batch > 1 && avail >= r_elems) {
+        const long long c = avail / r_elems;
+        chunk = int(c < batch ? c : batch);
+        if (chunk > kMaxChunk) chunk = kMaxChunk;
+    }
+    float2* Rregion = Q + q_elems;
+
+    CUtensorMap qmap;
+    e = qmap_fn(W)(Q, H, &qmap);
+    if (e != cudaSuccess) return cuda_fail(e, "encoding the intermediate's tensor map");
     ColFn col = col_fn(H);
     R2cFn r2c = r2c_fn(W);
     C2rFn c2r = c2r_fn(W);
 
     if (g_timer.on) g_timer.device = device;
-    for (int t = 0; t < batch; ++t) {
-        const float* tmpl = input + (size_t)t * sy * sx;
-        float* out = output + (size_t)t * oy * ox;
-        int m = timer_mark(s);
-        e = r2c(tmpl, slice, twW, sy, sx, H, scale, nz_row, device, s);
-        if (e != cudaSuccess) return cuda_fail(e, "row r2c launch");
-        timer_close(0, m, s);
-        m = timer_mark(s);
-        e = col(slice, spec, twH, sy, W2, oy, conj, nz_col, device, s);
-        if (e != cudaSuccess) return cuda_fail(e, "column launch");
-        timer_close(1, m, s);
-        m = timer_mark(s);
-        e = c2r(slice, out, twW, H, oy, ox, ox, device, s);
-        if (e != cudaSuccess) return cuda_fail(e, "row c2r launch");
-        timer_close(2, m, s);
+    const int step = chunk > 0 ? chunk : 1;
+    for (int t0 = 0; t0 < batch; t0 += step) {
+        const int n = batch - t0 < step ? batch - t0 : step;
+        int m = -1;
+        if (chunk > 0) {
+            m = timer_mark(s);
+            e = r2c(input + (size_t)t0 * sy * sx, Rregion, twW, sy, sx, (int)h_pad, r_elems, n,
+                    scale, nz_row, device, s);
+            if (e != cudaSuccess) return cuda_fail(e, "row r2c launch");
+            timer_close(0, m, s);
+        }
+        for (int j = 0; j < n; ++j) {
+            const int t = t0 + j;
+            const float2* Rt = Q;
+            int r_pitch = H;
+            if (chunk > 0) {
+                Rt = Rregion + (size_t)j * r_elems;
+                r_pitch = (int)h_pad;
+            } else {
+                m = timer_mark(s);
+                e = r2c(input + (size_t)t * sy * sx, Q, twW, sy, sx, H, 0, 1, scale, nz_row, device, s);
+                if (e != cudaSuccess) return cuda_fail(e, "row r2c launch");
+                timer_close(0, m, s);
+            }
+            m = timer_mark(s);
+            e = col(Q, Rt, r_pitch, spec, twH, sy, W2, oy, conj, nz_col, status, device, s);
+            if (e != cudaSuccess) return cuda_fail(e, "column launch");
+            timer_close(1, m, s);
+            m = timer_mark(s);
+            e = c2r(&qmap, output + (size_t)t * oy * ox, twW, oy, ox, ox, status, device, s);
+            if (e != cudaSuccess) return cuda_fail(e, "row c2r launch");
+            timer_close(2, m, s);
+        }
     }
     return ZFFT_SUCCESS;
 }
@@ -292,7 +354,59 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
 }  // namespace
 
 namespace zf {
+
 int plan_first_radix(int n) { return make_plan(n).R[0]; }
+
+cudaError_t encode_tensor_map_2d(CUtensorMap* map, const void* base, unsigned long long dim0,
+                                 unsigned long long dim1, unsigned long long stride1_bytes,
+                                 unsigned box0, unsigned box1) {
+    static std::once_flag once;
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    static cudaError_t lookup_err = cudaSuccess;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        lookup_err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled",
+                                             reinterpret_cast<void**>(&encode), cudaEnableDefault, &q);
+        if (lookup_err == cudaSuccess && q != cudaDriverEntryPointSuccess)
+            lookup_err = cudaErrorSymbolNotFound;
+    });
+    if (lookup_err != cudaSuccess) return lookup_err;
+    cuuint64_t dims[2] = {dim0, dim1};
+    cuuint64_t strides[1] = {stride1_bytes};
+    cuuint32_t box[2] = {box0, box1};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT64, 2, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// Bounded-wait self-test: the barrier expects 64 bytes but the single copy
+// delivers 16, so the phase never completes; the wait must give up after
+// `limit` cycles and report a timeout.  The copy itself has landed long
+// before the limit, so nothing is in flight when the block exits.
+__global__ void k_wait_selftest(int* status, long long limit) {
+    __shared__ __align__(16) float4 dst[4];
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_init_fence();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(&bar, 64);
+        tma_load_1d(dst, &g_selftest_src, 16, &bar);
+    }
+    const bool ok = mbar_wait_bounded(&bar, 0, limit);
+    if (__syncthreads_or(!ok) && threadIdx.x == 0) atomicExch(status, kStatusTimeout);
+}
+
+cudaError_t launch_wait_selftest(int* status, long long limit_cycles, cudaStream_t s) {
+    k_wait_selftest<<<1, 32, 0, s>>>(status, limit_cycles);
+    return cudaGetLastError();
+}
+
 }  // namespace zf
 
 extern "C" {
@@ -356,5 +470,50 @@ int zfft_stage_timing_read(double* ms, int* launches, int n) {
 }
 
 int zfft_get_version(void) { return kVersion; }
+
+int zfft_check_device_status(int device, void* stream, int* status) {
+    g_last_error.clear();
+    if (!status) return fail(ZFFT_ERROR_INVALID_VALUE, "status pointer is null");
+    *status = ZFFT_SUCCESS;
+    int ndev = 0;
+    cudaError_t e = cudaGetDeviceCount(&ndev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+    if (device < 0 || device >= ndev || device >= kMaxDevices)
+        return fail(ZFFT_ERROR_INVALID_VALUE, "invalid device index %d (%d devices)", device, ndev);
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess) return cuda_fail(guard.err, "cudaSetDevice");
+    int rc = ensure_device(device);
+    if (rc != ZFFT_SUCCESS) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+    int value = 0;
+    e = cudaMemcpy(&value, g_dev_status[device], sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "reading the device status word");
+    if (value != 0) {
+        const int zero = 0;
+        e = cudaMemcpy(g_dev_status[device], &zero, sizeof(int), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return cuda_fail(e, "clearing the device status word");
+    }
+    *status = value;
+    return ZFFT_SUCCESS;
+}
+
+int zfft_selftest_wait_timeout(int device, void* stream) {
+    g_last_error.clear();
+    int ndev = 0;
+    cudaError_t e = cudaGetDeviceCount(&ndev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+    if (device < 0 || device >= ndev || device >= kMaxDevices)
+        return fail(ZFFT_ERROR_INVALID_VALUE, "invalid device index %d (%d devices)", device, ndev);
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess) return cuda_fail(guard.err, "cudaSetDevice");
+    int rc = ensure_device(device);
+    if (rc != ZFFT_SUCCESS) return rc;
+    // ~1 ms at 2 GHz
+    e = zf::launch_wait_selftest(g_dev_status[device], 2000000LL, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "self-test launch");
+    return ZFFT_SUCCESS;
+}
 
 }  // extern "C"

@@ -415,16 +415,31 @@ struct Stockham {
         }
     }
 
+    // Offsets of element r within a butterfly fold into one padded base when
+    // the element stride is a multiple of 16 (spad(x + r*S) = spad(x) + r*spad(S)),
+    // or when the whole butterfly lies inside one 16-element block.
+    static constexpr bool load_folds(int s) { return nbf(s) % 16 == 0; }
+    static constexpr bool store_folds(int s) {
+        return ns(s) % 16 == 0 || (16 % (ns(s) * radix(s)) == 0);
+    }
+    static constexpr int store_off(int s) { return ns(s) % 16 == 0 ? ns(s) + ns(s) / 16 : ns(s); }
+
     // Read the inputs of stage s from the shared buffer.
     template <int s>
     ZF_DEV static void load(float2 (&v)[MAXE], const float2* buf, int t) {
         constexpr int R = radix(s), NB = nbf(s);
 #pragma unroll
         for (int q = 0; q < bpt(s); ++q) {
-            int b = t + q * T;
+            const int b = t + q * T;
             if (even(s) || b < NB) {
+                if constexpr (load_folds(s)) {
+                    const float2* p = buf + spad(b);
 #pragma unroll
-                for (int r = 0; r < R; ++r) v[q * R + r] = buf[spad(b + r * NB)];
+                    for (int r = 0; r < R; ++r) v[q * R + r] = p[r * (NB + NB / 16)];
+                } else {
+#pragma unroll
+                    for (int r = 0; r < R; ++r) v[q * R + r] = buf[spad(b + r * NB)];
+                }
             }
         }
     }
@@ -435,11 +450,17 @@ struct Stockham {
         constexpr int R = radix(s), NB = nbf(s), NS = ns(s);
 #pragma unroll
         for (int q = 0; q < bpt(s); ++q) {
-            int b = t + q * T;
+            const int b = t + q * T;
             if (even(s) || b < NB) {
-                int base = (b / NS) * NS * R + (b % NS);
+                const int base = (b / NS) * NS * R + (b % NS);
+                if constexpr (store_folds(s)) {
+                    float2* p = buf + spad(base);
 #pragma unroll
-                for (int r = 0; r < R; ++r) buf[spad(base + r * NS)] = v[q * R + r];
+                    for (int r = 0; r < R; ++r) p[r * store_off(s)] = v[q * R + r];
+                } else {
+#pragma unroll
+                    for (int r = 0; r < R; ++r) buf[spad(base + r * NS)] = v[q * R + r];
+                }
             }
         }
     }

@@ -1,6 +1,7 @@
 // Kernel instantiations and launchers for one FFT size.  Compiled once per
 // size with -DZF_SIZE=<n> (the build runs these compilations in parallel); each
-// object defines launch_col_<n>, launch_row_r2c_<n> and launch_row_c2r_<n>.
+// object defines launch_row_r2c_<n>, launch_col_<n>, make_qmap_<n> and
+// launch_row_c2r_<n>.
 //
 // Replaces the per-configuration template instantiation of zipFFT's launcher
 // (src/cuda/real_conv_2d.cuh:153-293 and the compile-time shape table in
@@ -48,45 +49,49 @@ cudaError_t configure(Kern kernel, KernelState& st, int smem, int threads, int d
 
 inline int min_int(int a, int b) { return a < b ? a : b; }
 
+template <int W2, int NZ>
+cudaError_t r2c_t(const float* tmpl, float2* R, const float2* tw, int h, int w, int r_pitch,
+                  long long r_tstride, int ntemplates, float scale, int device, cudaStream_t s) {
+    using C = R2cCfg<W2>;
+    static KernelState st;
+    auto kernel = k_row_r2c<W2, NZ>;
+    int cap = 0;
+    cudaError_t e = configure(kernel, st, C::SMEM, C::THREADS, device, &cap);
+    if (e != cudaSuccess) return e;
+    // Blocks per template: enough to fill the GPU over the whole chunk.
+    const int groups = (h + C::RPB - 1) / C::RPB;
+    const int per_t = min_int(groups, (cap + ntemplates - 1) / ntemplates);
+    dim3 grid(per_t > 0 ? per_t : 1, ntemplates);
+    kernel<<<grid, C::THREADS, C::SMEM, s>>>(tmpl, R, tw, h, w, r_pitch, r_tstride, scale);
+    return cudaGetLastError();
+}
+
 template <int H, bool CONJ, int NZ>
-cudaError_t col_t(float2* ws, const float2* spec, const float2* tw, int h, int W2, int store_rows,
-                  int device, cudaStream_t s) {
-    using C = ColCfg<H>;
+cudaError_t col_t(float2* Q, const float2* R, int r_pitch, const float2* spec, const float2* tw,
+                  int h, int W2, int store_rows, int* status, int device, cudaStream_t s) {
+    using C = ColCfg<H, NZ>;
     static KernelState st;
     auto kernel = k_col_fused<H, CONJ, NZ>;
     int cap = 0;
     cudaError_t e = configure(kernel, st, C::SMEM, C::THREADS, device, &cap);
     if (e != cudaSuccess) return e;
     const int grid = min_int((W2 + 1 + C::FPB - 1) / C::FPB, cap);
-    kernel<<<grid, C::THREADS, C::SMEM, s>>>(ws, spec, tw, h, W2, store_rows);
-    return cudaGetLastError();
-}
-
-template <int W2, int NZ>
-cudaError_t r2c_t(const float* tmpl, float2* ws, const float2* tw, int h, int w, int H,
-                  float scale, int device, cudaStream_t s) {
-    using C = RowCfg<W2>;
-    static KernelState st;
-    auto kernel = k_row_r2c<W2, NZ>;
-    int cap = 0;
-    cudaError_t e = configure(kernel, st, C::SMEM, C::THREADS, device, &cap);
-    if (e != cudaSuccess) return e;
-    const int grid = min_int((h + C::RPB - 1) / C::RPB, cap);
-    kernel<<<grid, C::THREADS, C::SMEM, s>>>(tmpl, ws, tw, h, w, H, scale);
+    kernel<<<grid, C::THREADS, C::SMEM, s>>>(Q, R, r_pitch, spec, tw, h, W2, store_rows, status);
     return cudaGetLastError();
 }
 
 template <int W2>
-cudaError_t c2r_t(const float2* ws, float* out, const float2* tw, int H, int out_rows,
-                  int out_cols, int out_pitch, int device, cudaStream_t s) {
-    using C = RowCfg<W2>;
+cudaError_t c2r_t(const CUtensorMap* qmap, float* out, const float2* tw, int out_rows,
+                  int out_cols, int out_pitch, int* status, int device, cudaStream_t s) {
+    using C = C2rCfg<W2>;
     static KernelState st;
     auto kernel = k_row_c2r<W2>;
     int cap = 0;
     cudaError_t e = configure(kernel, st, C::SMEM, C::THREADS, device, &cap);
     if (e != cudaSuccess) return e;
-    const int grid = min_int((out_rows + C::RPB - 1) / C::RPB, cap);
-    kernel<<<grid, C::THREADS, C::SMEM, s>>>(ws, out, tw, H, out_rows, out_cols, out_pitch);
+    const int groups = (out_rows + C::RPB - 1) / C::RPB;
+    const int grid = min_int(groups, cap);
+    kernel<<<grid, C::THREADS, C::SMEM, s>>>(*qmap, out, tw, out_rows, out_cols, out_pitch, status);
     return cudaGetLastError();
 }
 
@@ -99,37 +104,43 @@ constexpr bool kPruned = ZF_SIZE >= 1024;
 #define ZF_CAT2(a, b) a##b
 #define ZF_CAT(a, b) ZF_CAT2(a, b)
 
-cudaError_t ZF_CAT(launch_col_, ZF_SIZE)(float2* ws, const float2* spec, const float2* tw, int h,
-                                         int W2, int store_rows, bool conj, int nz, int device,
-                                         cudaStream_t s) {
-    constexpr int H = ZF_SIZE;
-    if constexpr (kPruned) {
-        if (nz == 1)
-            return conj ? col_t<H, true, 1>(ws, spec, tw, h, W2, store_rows, device, s)
-                        : col_t<H, false, 1>(ws, spec, tw, h, W2, store_rows, device, s);
-        if (nz == 2)
-            return conj ? col_t<H, true, 2>(ws, spec, tw, h, W2, store_rows, device, s)
-                        : col_t<H, false, 2>(ws, spec, tw, h, W2, store_rows, device, s);
-    }
-    return conj ? col_t<H, true, 0>(ws, spec, tw, h, W2, store_rows, device, s)
-                : col_t<H, false, 0>(ws, spec, tw, h, W2, store_rows, device, s);
-}
-
-cudaError_t ZF_CAT(launch_row_r2c_, ZF_SIZE)(const float* tmpl, float2* ws, const float2* tw,
-                                             int h, int w, int H, float scale, int nz, int device,
+cudaError_t ZF_CAT(launch_row_r2c_, ZF_SIZE)(const float* tmpl, float2* R, const float2* tw, int h,
+                                             int w, int r_pitch, long long r_tstride,
+                                             int ntemplates, float scale, int nz, int device,
                                              cudaStream_t s) {
     constexpr int W2 = ZF_SIZE / 2;
     if constexpr (kPruned) {
-        if (nz == 1) return r2c_t<W2, 1>(tmpl, ws, tw, h, w, H, scale, device, s);
-        if (nz == 2) return r2c_t<W2, 2>(tmpl, ws, tw, h, w, H, scale, device, s);
+        if (nz == 1) return r2c_t<W2, 1>(tmpl, R, tw, h, w, r_pitch, r_tstride, ntemplates, scale, device, s);
+        if (nz == 2) return r2c_t<W2, 2>(tmpl, R, tw, h, w, r_pitch, r_tstride, ntemplates, scale, device, s);
     }
-    return r2c_t<W2, 0>(tmpl, ws, tw, h, w, H, scale, device, s);
+    return r2c_t<W2, 0>(tmpl, R, tw, h, w, r_pitch, r_tstride, ntemplates, scale, device, s);
 }
 
-cudaError_t ZF_CAT(launch_row_c2r_, ZF_SIZE)(const float2* ws, float* out, const float2* tw, int H,
-                                             int out_rows, int out_cols, int out_pitch, int device,
-                                             cudaStream_t s) {
-    return c2r_t<ZF_SIZE / 2>(ws, out, tw, H, out_rows, out_cols, out_pitch, device, s);
+cudaError_t ZF_CAT(launch_col_, ZF_SIZE)(float2* Q, const float2* R, int r_pitch,
+                                         const float2* spec, const float2* tw, int h, int W2,
+                                         int store_rows, bool conj, int nz, int* status,
+                                         int device, cudaStream_t s) {
+    constexpr int H = ZF_SIZE;
+#define ZF_COL(CJ, NZV) col_t<H, CJ, NZV>(Q, R, r_pitch, spec, tw, h, W2, store_rows, status, device, s)
+    if constexpr (kPruned) {
+        if (nz == 1) return conj ? ZF_COL(true, 1) : ZF_COL(false, 1);
+        if (nz == 2) return conj ? ZF_COL(true, 2) : ZF_COL(false, 2);
+    }
+    return conj ? ZF_COL(true, 0) : ZF_COL(false, 0);
+#undef ZF_COL
+}
+
+cudaError_t ZF_CAT(make_qmap_, ZF_SIZE)(const float2* Q, int H, CUtensorMap* map) {
+    using C = C2rCfg<ZF_SIZE / 2>;
+    // Q is column-major: dim 0 = rows y (H, contiguous), dim 1 = packed columns.
+    return encode_tensor_map_2d(map, Q, (unsigned long long)H, (unsigned long long)(ZF_SIZE / 2),
+                                (unsigned long long)H * 8ull, C::RPB, C::BOXK);
+}
+
+cudaError_t ZF_CAT(launch_row_c2r_, ZF_SIZE)(const CUtensorMap* qmap, float* out, const float2* tw,
+                                             int out_rows, int out_cols, int out_pitch,
+                                             int* status, int device, cudaStream_t s) {
+    return c2r_t<ZF_SIZE / 2>(qmap, out, tw, out_rows, out_cols, out_pitch, status, device, s);
 }
 
 }  // namespace zf

@@ -1,6 +1,7 @@
 // Internal launch entry points, one set per FFT size (defined in inst.cu,
 // compiled once per size).  Not part of the public C ABI.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 
@@ -8,26 +9,37 @@
 
 namespace zf {
 
-// Column pass of an H-row image: forward FFT of the h non-zero rows of every
-// packed column, product with the spectrum, inverse FFT, first store_rows rows
-// stored in place.  nz: 1 or 2 when the non-zero rows fit the first 1 or 2
+// Row r2c of `ntemplates` templates (h x w each, consecutive in tmpl) of a
+// W-column image: R of template j at R + j * r_tstride, element (kx, n) at
+// kx * r_pitch + n.  nz: 1 or 2 when the template row fits the first 1 or 2
 // stage-0 inputs of every butterfly, else 0.
-#define ZF_DECL_COL(N)                                                                       \
-    cudaError_t launch_col_##N(float2* ws, const float2* spec, const float2* tw, int h, int W2, \
-                               int store_rows, bool conj, int nz, int device, cudaStream_t s);
-// Row passes of a W-column image (FFT length W, folded to W/2 complex).
-#define ZF_DECL_ROW(N)                                                                         \
-    cudaError_t launch_row_r2c_##N(const float* tmpl, float2* ws, const float2* tw, int h,      \
-                                   int w, int H, float scale, int nz, int device, cudaStream_t s); \
-    cudaError_t launch_row_c2r_##N(const float2* ws, float* out, const float2* tw, int H,       \
-                                   int out_rows, int out_cols, int out_pitch, int device,        \
-                                   cudaStream_t s);
-ZF_FOR_EACH_FFT_SIZE(ZF_DECL_COL)
-ZF_FOR_EACH_FFT_SIZE(ZF_DECL_ROW)
-#undef ZF_DECL_COL
-#undef ZF_DECL_ROW
+// Column pass of an H-row image: forward FFT of the h rows of R, product with
+// the spectrum, inverse FFT, first store_rows rows of Q stored.
+// Row c2r: the Q tile map comes from make_qmap_<W> (same W); out_rows rows of
+// out_cols values at out_pitch.
+#define ZF_DECL(N)                                                                              \
+    cudaError_t launch_row_r2c_##N(const float* tmpl, float2* R, const float2* tw, int h, int w, \
+                                   int r_pitch, long long r_tstride, int ntemplates, float scale, \
+                                   int nz, int device, cudaStream_t s);                          \
+    cudaError_t launch_col_##N(float2* Q, const float2* R, int r_pitch, const float2* spec,      \
+                               const float2* tw, int h, int W2, int store_rows, bool conj, int nz, \
+                               int* status, int device, cudaStream_t s);                         \
+    cudaError_t make_qmap_##N(const float2* Q, int H, CUtensorMap* map);                        \
+    cudaError_t launch_row_c2r_##N(const CUtensorMap* qmap, float* out, const float2* tw,        \
+                                   int out_rows, int out_cols, int out_pitch, int* status,       \
+                                   int device, cudaStream_t s);
+ZF_FOR_EACH_FFT_SIZE(ZF_DECL)
+#undef ZF_DECL
 
 // First radix of the plan of an n-point transform (host side, for nz).
 int plan_first_radix(int n);
+
+// Encode a 2D tiled tensor map (driver entry point resolved once).
+cudaError_t encode_tensor_map_2d(CUtensorMap* map, const void* base, unsigned long long dim0,
+                                 unsigned long long dim1, unsigned long long stride1_bytes,
+                                 unsigned box0, unsigned box1);
+
+// Launch of the bounded-wait self-test kernel (capi.cu).
+cudaError_t launch_wait_selftest(int* status, long long limit_cycles, cudaStream_t s);
 
 }  // namespace zf

@@ -4,38 +4,40 @@
 // Per template, with image size H x W, template h x w and W2 = W/2:
 //
 //   k_row_r2c   rows n < h:  X_n = rfft_W(pad(t_n)) * 1/(H W)      (cuh:8-30)
-//               written as R[kx][n] (column-major, packed kx = 0..W2-1)
-//   k_col_fused columns kx:  Q[.,kx] = IFFT_H( conj(FFT_H(pad_h(R[kx]))) . S[kx] )
+//               stored column-major as R[kx][n], packed kx = 0..W2-1
+//   k_col_fused columns kx:  Q[., kx] = IFFT_H( conj(FFT_H(pad_h(R[kx]))) . S[kx] )
 //                                                                   (cuh:58-117)
-//   k_row_c2r   rows y:      out[y] = irfft_W(Q[y, .])              (cuh:34-56)
+//   k_row_c2r   rows y:      out[y] = irfft_W(Q[y, .]), cropped       (cuh:34-56)
 //
-// Layout of the per-template workspace slice (complex64, column pitch H):
-//   element (kx, y) at kx * H + y, packed kx in [0, W2).  Packed column 0
-//   holds the two real columns kx = 0 (real part) and kx = W2 (imaginary part).
-//   R occupies rows [0, h) of every column; the column kernel replaces it in
-//   place by Q, one column per transform, so no two blocks touch the same
-//   column.  The slice needs H * W2 complex values, less than the
-//   H * (W/2 + 1) the reference's workspace holds per template
-//   (real_conv_2d_binding.cu:235-245).
+// Intermediate layout (complex64): Q is column-major, element (kx, y) at
+// kx * H + y, packed kx in [0, W2), so one H x W2 slice holds a template's
+// intermediate (the reference's workspace holds H x (W/2+1) per template,
+// real_conv_2d_binding.cu:235-245).  Packed column 0 carries the two real
+// columns kx = 0 (real part) and kx = W/2 (imaginary part).  R either sits in
+// rows [0, h) of the same slice (pitch H; the column kernel then overwrites it
+// in place, each column by the block that read it) or in a separate region
+// with pitch round_up(h, 2) so that the row kernel can run several templates
+// per launch.
 //
-// Differences from the reference's layout (real_conv_2d_io.hpp:134-195): the
-// reference keeps the workspace row-major and reads it down columns at stride
-// W/2+1; here the column kernel reads and writes whole contiguous columns and
-// the row kernels move 4 rows at a time so each column segment they touch is
-// one 32-byte sector.
-//
-// The normalisations 1/H (io.hpp:278-282) and 1/W (io.hpp:302-306) are folded
-// into the template rows (k_row_r2c), so the column and row-inverse kernels do
-// no scaling.
+// Differences from the reference's data movement (io.hpp:134-195, which reads
+// a row-major workspace down its columns at stride W/2+1):
+//   * the column kernel streams whole contiguous columns: the image spectrum
+//     column and the template column arrive by TMA bulk copies into shared
+//     memory, double-buffered across the block's loop over columns;
+//   * the inverse row kernel fetches 2-row x 256-column tiles of Q with 2D TMA
+//     tensor loads (the transpose happens in the copy engine);
+//   * the normalisations 1/H (io.hpp:278-282) and 1/W (io.hpp:302-306) are
+//     folded into the template rows, so later kernels do no scaling.
 #pragma once
 
+#include "async_copy.cuh"
 #include "fft_core.cuh"
 
 namespace zf {
 
 #if defined(__CUDACC__)
 ZF_DEV float2* dyn_smem() {
-    extern __shared__ __align__(16) float2 zf_dyn_smem_arr[];
+    extern __shared__ __align__(128) float2 zf_dyn_smem_arr[];
     return zf_dyn_smem_arr;
 }
 #else
@@ -44,24 +46,12 @@ float2* dyn_smem();  // provided by the CPU test harness
 
 // Threads per transform: 16 elements per thread in radix-16 stages.
 constexpr int fft_threads(int n) { return (n + 15) / 16; }
-
-template <int H>
-struct ColCfg {
-    static constexpr int T = fft_threads(H);
-    static constexpr int FPB = T >= 256 ? 1 : 256 / T;  // columns per block
-    static constexpr int THREADS = FPB * T;
-    static constexpr int BUF = spad_size(H);  // float2 per column buffer
-    static constexpr int SMEM = FPB * BUF * 8;
-};
-
-template <int W2>
-struct RowCfg {
-    static constexpr int T = fft_threads(W2);
-    static constexpr int RPB = (256 / T) > 4 ? 256 / T : 4;  // rows per block
-    static constexpr int THREADS = RPB * T;
-    static constexpr int BUF = spad_size(W2);
-    static constexpr int SMEM = RPB * BUF * 8;
-};
+constexpr int round_up(int x, int m) { return (x + m - 1) / m * m; }
+constexpr int cmax(int a, int b) { return a > b ? a : b; }
+// Padded exchange buffer length, = 4 (mod 16): buffers of consecutive rows then
+// start 8 banks apart, so the split passes (which walk 4 rows in lockstep)
+// are bank-conflict free.
+constexpr int xbuf_len(int n) { return round_up(spad_size(n) - 4, 16) + 4; }
 
 // True when the radix sequence of n reads the same backwards.  The column
 // kernel's inverse runs the radices in reverse, so for such plans it can use
@@ -73,47 +63,37 @@ constexpr bool plan_palindrome(int n) {
     return true;
 }
 
-// ---------------------------------------------------------------------------
-// Loaders: the implicit zero padding (io.hpp:69-100, :134-166).  Indices past
-// the signal end return zero without a memory access.
-// ---------------------------------------------------------------------------
-
-// Column input: h complex rows of one packed column.  mode 0: the complex
-// column; mode 1 / 2: the real / imaginary part taken as a real column (the
-// kx = 0 and kx = W/2 columns share packed column 0).
-struct ColLoader {
-    const float2* src;
-    int h;
-    int mode;
-    ZF_DEV float2 operator()(int i) const {
-        if (i >= h) return c_make(0.f, 0.f);
-        if (mode == 0) return src[i];
-        const float* f = reinterpret_cast<const float*>(src + i);
-        return c_make(mode == 1 ? f[0] : f[1], 0.f);
-    }
+// ===========================================================================
+// Kernel 1: forward real FFT of template rows (W2-point complex FFT of
+// z[m] = x[2m] + i x[2m+1] plus the split post-pass), packed and scaled.
+// grid.y indexes templates; blocks loop over row groups of one template.
+// ===========================================================================
+template <int W2>
+struct R2cCfg {
+    static constexpr int T = fft_threads(W2);
+    static constexpr int RPB = cmax(4, 256 / T);  // rows per block
+    static constexpr int THREADS = RPB * T;
+    static constexpr int XB = xbuf_len(W2);
+    static constexpr int SMEM = RPB * XB * 8;
 };
 
-// Row input for the folded real FFT: z[m] = x[2m] + i x[2m+1], x zero past w.
+// Row input for the folded real FFT, zero past the template width.
 struct RowLoader {
     const float* row;
     int w;
     ZF_DEV float2 operator()(int m) const {
-        int i = 2 * m;
-        float a = i < w ? __ldg(row + i) : 0.f;
-        float b = i + 1 < w ? __ldg(row + i + 1) : 0.f;
+        const int i = 2 * m;
+        const float a = i < w ? __ldg(row + i) : 0.f;
+        const float b = i + 1 < w ? __ldg(row + i + 1) : 0.f;
         return c_make(a, b);
     }
 };
 
-// ---------------------------------------------------------------------------
-// Kernel 1: forward real FFT of the template rows, folded into a W2-point
-// complex FFT plus the split post-pass; output packed and scaled by `scale`.
-// ---------------------------------------------------------------------------
 template <int W2, int NZ>
-__global__ void __launch_bounds__(RowCfg<W2>::THREADS)
-    k_row_r2c(const float* __restrict__ tmpl, float2* __restrict__ ws,
-              const float2* __restrict__ twW, int h, int w, int H, float scale) {
-    using C = RowCfg<W2>;
+__global__ void __launch_bounds__(R2cCfg<W2>::THREADS)
+    k_row_r2c(const float* __restrict__ tmpl, float2* __restrict__ R, const float2* __restrict__ twW,
+              int h, int w, int r_pitch, long long r_tstride, float scale) {
+    using C = R2cCfg<W2>;
     using F = Stockham<W2, C::T, false, false>;
     static_assert(F::S >= 2, "row FFT needs at least two stages");
     constexpr int RL = F::radix(F::S - 1), NBL = F::nbf(F::S - 1);
@@ -121,20 +101,23 @@ __global__ void __launch_bounds__(RowCfg<W2>::THREADS)
     const int tid = threadIdx.x;
     const int g = tid / C::T, t = tid % C::T;
     float2* smem = dyn_smem();
-    float2* buf = smem + g * C::BUF;
+    float2* buf = smem + g * C::XB;
+    const float* tm = tmpl + (size_t)blockIdx.y * h * w;
+    float2* Rt = R + (size_t)blockIdx.y * r_tstride;
 
     typename F::Twiddles tw;
     F::template load_twiddles<2 * W2>(tw, twW, t);
 
     for (int n0 = blockIdx.x * C::RPB; n0 < h; n0 += gridDim.x * C::RPB) {
         const int n = n0 + g;
-        RowLoader ld{tmpl + (size_t)(n < h ? n : 0) * w, n < h ? w : 0};
+        RowLoader ld{tm + (size_t)(n < h ? n : 0) * w, n < h ? w : 0};
         float2 v[F::MAXE];
         F::template run_loader<NZ>(v, ld, buf, tw, t);
-        // Z in natural order into the buffer.
+        // Z in natural order into the buffer (all reads of the buffer by the
+        // last stage completed at run_loader's final barrier).
 #pragma unroll
         for (int q = 0; q < F::bpt(F::S - 1); ++q) {
-            int b = t + q * C::T;
+            const int b = t + q * C::T;
             if (F::even(F::S - 1) || b < NBL) {
 #pragma unroll
                 for (int r = 0; r < RL; ++r) buf[spad(b + r * NBL)] = v[q * RL + r];
@@ -143,17 +126,17 @@ __global__ void __launch_bounds__(RowCfg<W2>::THREADS)
         __syncthreads();
         // Split pass: X[k] = E[k] + w^k O[k], X[W2-k] = conj(E[k] - w^k O[k]),
         // E = (Z[k] + conj Z[W2-k]) / 2, O = (Z[k] - conj Z[W2-k]) / 2i.
-        // Items (k, row) with the row index fastest, so each store of a column
+        // Items (k, row) run with the row fastest so each store of a column
         // segment R[k][n0 .. n0+RPB) is contiguous.
         constexpr int NIT = (W2 / 2 + 1) * C::RPB;
         for (int it = tid; it < NIT; it += C::THREADS) {
             const int nl = it % C::RPB, k = it / C::RPB;
             const int nn = n0 + nl;
             if (nn >= h) continue;
-            const float2* zb = smem + nl * C::BUF;
+            const float2* zb = smem + nl * C::XB;
             const float2 A = zb[spad(k)];
             if (k == 0) {
-                ws[nn] = c_make((A.x + A.y) * scale, (A.x - A.y) * scale);
+                Rt[nn] = c_make((A.x + A.y) * scale, (A.x - A.y) * scale);
                 continue;
             }
             const float2 B = zb[spad(W2 - k)];
@@ -161,27 +144,44 @@ __global__ void __launch_bounds__(RowCfg<W2>::THREADS)
             const float2 G = c_make(0.5f * (A.x - B.x), 0.5f * (A.y + B.y));  // (A - conj B)/2
             const float2 wk = __ldg(twW + k);
             const float2 Ow = c_mul(c_make(G.y, -G.x), wk);  // w^k * G / i
-            ws[(size_t)k * H + nn] = c_scale(c_add(E, Ow), scale);
-            if (2 * k != W2) ws[(size_t)(W2 - k) * H + nn] = c_scale(c_conj(c_sub(E, Ow)), scale);
+            Rt[(size_t)k * r_pitch + nn] = c_scale(c_add(E, Ow), scale);
+            if (2 * k != W2) Rt[(size_t)(W2 - k) * r_pitch + nn] = c_scale(c_conj(c_sub(E, Ow)), scale);
         }
         __syncthreads();
     }
 }
 
-// ---------------------------------------------------------------------------
+// ===========================================================================
 // Kernel 2: per packed column, forward FFT over H of the h non-zero rows,
-// multiply by the conjugate (correlation) or plain (convolution) image
-// spectrum column, inverse FFT, store the first store_rows rows in place.
-// The block loops over columns; virtual column vc in [0, W2] is
-//   vc = 0      : real column kx = 0   (real part of packed column 0)
-//   vc = W2     : real column kx = W/2 (imaginary part of packed column 0)
-//   otherwise   : complex column kx = vc.
-// ---------------------------------------------------------------------------
+// product with the conjugate (correlation) or plain (convolution) image
+// spectrum column, inverse FFT, first store_rows rows stored.
+//
+// Virtual column vc in [0, W2]: vc = 0 is the real column kx = 0 (real part of
+// packed column 0), vc = W2 the real column kx = W/2 (its imaginary part),
+// otherwise the complex column kx = vc.  A block holds FPB columns; it loops
+// over column groups, prefetching the next group's spectrum and template
+// columns by TMA while it transforms the current one.
+// ===========================================================================
+template <int H, int NZ>
+struct ColCfg {
+    static constexpr int T = fft_threads(H);
+    static constexpr int FPB = T >= 128 ? 1 : 128 / T;  // columns per block
+    static constexpr int THREADS = FPB * T;
+    static constexpr int MINB = cmax(1, 512 / THREADS);  // blocks per SM targeted
+    static constexpr int XB = xbuf_len(H);
+    static constexpr int SB = round_up(H, 16);                     // spectrum column
+    static constexpr int NB0 = H / make_plan(H).R[0];
+    static constexpr int RB = round_up(NZ > 0 ? NZ * NB0 : H, 16);  // template column
+    static constexpr int FLOATS = FPB * (XB + 2 * SB + 2 * RB);
+    static constexpr int SMEM = FLOATS * 8 + 2 * 8;  // + two mbarriers
+};
+
 template <int H, bool CONJ, int NZ>
-__global__ void __launch_bounds__(ColCfg<H>::THREADS)
-    k_col_fused(float2* __restrict__ ws, const float2* __restrict__ spec,
-                const float2* __restrict__ twH, int h, int W2, int store_rows) {
-    using C = ColCfg<H>;
+__global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
+    k_col_fused(float2* __restrict__ Q, const float2* __restrict__ R, int r_pitch,
+                const float2* __restrict__ spec, const float2* __restrict__ twH, int h, int W2,
+                int store_rows, int* __restrict__ status) {
+    using C = ColCfg<H, NZ>;
     using F = Stockham<H, C::T, false, false>;
     using I = Stockham<H, C::T, true, true>;
     static_assert(F::S >= 2, "column FFT needs at least two stages");
@@ -191,7 +191,22 @@ __global__ void __launch_bounds__(ColCfg<H>::THREADS)
 
     const int tid = threadIdx.x;
     const int g = tid / C::T, t = tid % C::T;
-    float2* buf = dyn_smem() + g * C::BUF;
+    float2* smem = dyn_smem();
+    float2* xbuf = smem + g * C::XB;
+    float2* sbase = smem + C::FPB * C::XB;            // [2][FPB][SB]
+    float2* rbase = sbase + 2 * C::FPB * C::SB;       // [2][FPB][RB]
+    uint64_t* mbar = reinterpret_cast<uint64_t*>(rbase + 2 * C::FPB * C::RB);
+
+    // Template-column buffers are zero beyond h: the pruned start reads them
+    // unconditionally.  TMA later overwrites only the first round_up(h, 2).
+    for (int i = tid; i < 2 * C::FPB * C::RB; i += C::THREADS) rbase[i] = c_make(0.f, 0.f);
+    __syncthreads();
+    if (tid == 0) {  // after the zero fill: orders it before the first TMA write
+        mbar_init(&mbar[0], 1);
+        mbar_init(&mbar[1], 1);
+        mbar_init_fence();
+    }
+    __syncthreads();
 
     typename F::Twiddles twf;
     F::template load_twiddles<H>(twf, twH, t);
@@ -199,54 +214,104 @@ __global__ void __launch_bounds__(ColCfg<H>::THREADS)
     typename I::Twiddles twi_own;
     if constexpr (!kShare) I::template load_twiddles<H>(twi_own, twH, t);
 
-    for (int vc0 = blockIdx.x * C::FPB; vc0 <= W2; vc0 += gridDim.x * C::FPB) {
+    const uint32_t r_bytes = (uint32_t)round_up(h, 2) * 8u;
+    const int stride = gridDim.x * C::FPB;
+
+    // Thread 0 fetches the spectrum and template columns of group vc0 into buffer b.
+    auto issue = [&](int b, int vc0) {
+        uint32_t bytes = 0;
+        for (int j = 0; j < C::FPB; ++j)
+            if (vc0 + j <= W2) bytes += H * 8u + r_bytes;
+        mbar_arrive_expect_tx(&mbar[b], bytes);
+        for (int j = 0; j < C::FPB; ++j) {
+            const int vc = vc0 + j;
+            if (vc > W2) break;
+            tma_load_1d(sbase + (b * C::FPB + j) * C::SB, spec + (size_t)vc * H, H * 8u, &mbar[b]);
+            const int rc = vc == W2 ? 0 : vc;
+            tma_load_1d(rbase + (b * C::FPB + j) * C::RB, R + (size_t)rc * r_pitch, r_bytes,
+                        &mbar[b]);
+        }
+    };
+
+    int vc0 = blockIdx.x * C::FPB;
+    if (tid == 0 && vc0 <= W2) issue(0, vc0);
+    for (int it = 0; vc0 <= W2; ++it, vc0 += stride) {
+        const int b = it & 1;
+        const uint32_t parity = (it >> 1) & 1;
+        // The other buffer was last read before this iteration's barriers.
+        const bool more = vc0 + stride <= W2;
+        if (tid == 0 && more) issue(b ^ 1, vc0 + stride);
+        const bool ok = mbar_wait_bounded(&mbar[b], parity);
+        if (__syncthreads_or(!ok)) {
+            if (tid == 0) {
+                atomicExch(status, kStatusTimeout);
+                if (more) mbar_wait_bounded(&mbar[b ^ 1], ((it + 1) >> 1) & 1);
+            }
+            return;
+        }
+
         const int vc = vc0 + g;
         const bool active = vc <= W2;
         const int mode = vc == 0 ? 1 : (vc == W2 ? 2 : 0);
-        const size_t col = (size_t)(mode != 0 ? 0 : vc) * H;
-        ColLoader ld{ws + col, active ? h : 0, mode};
+        const float2* rcol = rbase + (b * C::FPB + g) * C::RB;
+        const float2* scol = sbase + (b * C::FPB + g) * C::SB;
 
         float2 v[F::MAXE];
-        F::template run_loader<NZ>(v, ld, buf, twf, t);
+        if (mode == 0) {
+            auto ld = [&](int i) { return i < h ? rcol[i] : c_make(0.f, 0.f); };
+            F::template run_loader<NZ>(v, ld, xbuf, twf, t);
+        } else {
+            const float* rf = reinterpret_cast<const float*>(rcol) + (mode == 2 ? 1 : 0);
+            auto ld = [&](int i) { return c_make(i < h ? rf[2 * i] : 0.f, 0.f); };
+            F::template run_loader<NZ>(v, ld, xbuf, twf, t);
+        }
 
         // Pointwise product with the image spectrum column (cuh:86-111).
-        const float2* sp = spec + (size_t)(active ? vc : 0) * H;
 #pragma unroll
         for (int q = 0; q < F::bpt(F::S - 1); ++q) {
-            int b = t + q * C::T;
-            if (F::even(F::S - 1) || b < NBL) {
+            const int bb = t + q * C::T;
+            if (F::even(F::S - 1) || bb < NBL) {
+                const float2* sp = scol + bb;
 #pragma unroll
                 for (int r = 0; r < RL; ++r) {
-                    float2 s = __ldg(sp + b + r * NBL);
-                    float2 a = v[q * RL + r];
+                    const float2 s = sp[r * NBL];
+                    const float2 a = v[q * RL + r];
                     v[q * RL + r] = CONJ ? c_conj_mul(a, s) : c_mul(a, s);
                 }
             }
         }
 
         if constexpr (kShare) {
-            I::run_regs(v, buf, twf, t);
+            I::run_regs(v, xbuf, twf, t);
         } else {
-            I::run_regs(v, buf, twi_own, t);
+            I::run_regs(v, xbuf, twi_own, t);
         }
 
         if (active) {
-            float2* dst = ws + col;
-            float* dstf = reinterpret_cast<float*>(dst);
+            const bool full = store_rows >= H;
+            if (mode == 0) {
+                float2* dst = Q + (size_t)vc * H;
 #pragma unroll
-            for (int q = 0; q < I::bpt(I::S - 1); ++q) {
-                int b = t + q * C::T;
-                if (I::even(I::S - 1) || b < NBO) {
+                for (int q = 0; q < I::bpt(I::S - 1); ++q) {
+                    const int bb = t + q * C::T;
+                    if (I::even(I::S - 1) || bb < NBO) {
 #pragma unroll
-                    for (int r = 0; r < RO; ++r) {
-                        int y = b + r * NBO;
-                        if (y < store_rows) {
-                            float2 o = v[q * RO + r];
-                            if (mode == 0) {
-                                dst[y] = o;
-                            } else {
-                                dstf[2 * y + (mode == 2 ? 1 : 0)] = o.x;
-                            }
+                        for (int r = 0; r < RO; ++r) {
+                            const int y = bb + r * NBO;
+                            if (full || y < store_rows) dst[y] = v[q * RO + r];
+                        }
+                    }
+                }
+            } else {
+                float* dstf = reinterpret_cast<float*>(Q) + (mode == 2 ? 1 : 0);
+#pragma unroll
+                for (int q = 0; q < I::bpt(I::S - 1); ++q) {
+                    const int bb = t + q * C::T;
+                    if (I::even(I::S - 1) || bb < NBO) {
+#pragma unroll
+                        for (int r = 0; r < RO; ++r) {
+                            const int y = bb + r * NBO;
+                            if (full || y < store_rows) dstf[2 * y] = v[q * RO + r].x;
                         }
                     }
                 }
@@ -255,67 +320,122 @@ __global__ void __launch_bounds__(ColCfg<H>::THREADS)
     }
 }
 
-// ---------------------------------------------------------------------------
-// Kernel 3: inverse real FFT of output rows, folded into a W2-point complex
-// inverse FFT after the split pre-pass; crops to out_cols columns.
-// ---------------------------------------------------------------------------
+// ===========================================================================
+// Kernel 3: inverse real FFT of output rows: the split pre-pass
+//   2Z[k] = (X[k] + conj X[W2-k]) + i w^-k (X[k] - conj X[W2-k])
+// is fused into the reads of the first stage; a W2-point complex inverse FFT
+// follows; z[m] = (out[2m], out[2m+1]).  Each block loops over groups of RPB
+// rows; a group's Q tile (all W2 columns x RPB rows) arrives by 2D TMA loads,
+// double-buffered.
+// ===========================================================================
+// Largest divisor of n not above 256 (the TMA box limit).
+constexpr int tma_box(int n) {
+    for (int d = 256; d >= 1; --d)
+        if (n % d == 0) return d;
+    return 1;
+}
+
 template <int W2>
-__global__ void __launch_bounds__(RowCfg<W2>::THREADS)
-    k_row_c2r(const float2* __restrict__ ws, float* __restrict__ out,
-              const float2* __restrict__ twW, int H, int out_rows, int out_cols,
-              int out_pitch) {
-    using C = RowCfg<W2>;
+struct C2rCfg {
+    static constexpr int T = fft_threads(W2);
+    static constexpr int RPB = cmax(2, 128 / T);  // rows per block (even: TMA x alignment)
+    static constexpr int THREADS = RPB * T;
+    static constexpr int MINB = cmax(1, 512 / THREADS);
+    static constexpr int XB = xbuf_len(W2);
+    static constexpr int BOXK = tma_box(W2);
+    static constexpr int QB = round_up(W2 * RPB, 16);  // one Q tile
+    static constexpr int FLOATS = 2 * QB + RPB * XB;
+    static constexpr int SMEM = FLOATS * 8 + 2 * 8;
+};
+
+template <int W2>
+__global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
+    k_row_c2r(const __grid_constant__ CUtensorMap qmap, float* __restrict__ out,
+              const float2* __restrict__ twW, int out_rows, int out_cols, int out_pitch,
+              int* __restrict__ status) {
+    using C = C2rCfg<W2>;
     using I = Stockham<W2, C::T, true, false>;
     static_assert(I::S >= 2, "row FFT needs at least two stages");
+    constexpr int R0 = I::radix(0), NB0 = I::nbf(0);
     constexpr int RL = I::radix(I::S - 1), NBL = I::nbf(I::S - 1);
+    static_assert((C::RPB * 8) % 16 == 0, "TMA inner box must be a multiple of 16 bytes");
 
     const int tid = threadIdx.x;
     const int g = tid / C::T, t = tid % C::T;
     float2* smem = dyn_smem();
-    float2* buf = smem + g * C::BUF;
+    float2* qbase = smem;                       // [2][W2][RPB]
+    float2* xbuf = smem + 2 * C::QB + g * C::XB;
+    uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + C::FLOATS);
+
+    if (tid == 0) {
+        mbar_init(&mbar[0], 1);
+        mbar_init(&mbar[1], 1);
+        mbar_init_fence();
+    }
+    __syncthreads();
 
     typename I::Twiddles tw;
     I::template load_twiddles<2 * W2>(tw, twW, t);
 
     const bool vec_ok = out_cols == 2 * W2 && (out_pitch % 2) == 0 &&
                         (reinterpret_cast<size_t>(out) % 8) == 0;
+    const int ngroups = (out_rows + C::RPB - 1) / C::RPB;
 
-    for (int y0 = blockIdx.x * C::RPB; y0 < out_rows; y0 += gridDim.x * C::RPB) {
-        // Split pre-pass: 2Z[k] = (X[k] + conj X[W2-k]) + i w^-k (X[k] - conj X[W2-k]).
-        constexpr int NIT = (W2 / 2 + 1) * C::RPB;
-        for (int it = tid; it < NIT; it += C::THREADS) {
-            const int yl = it % C::RPB, k = it / C::RPB;
-            const int y = y0 + yl;
-            if (y >= out_rows) continue;
-            float2* zb = smem + yl * C::BUF;
-            const float2 A = ws[(size_t)k * H + y];
-            if (k == 0) {  // packed (X[0], X[W2])
-                zb[spad(0)] = c_make(A.x + A.y, A.x - A.y);
-                continue;
+    auto issue = [&](int b, int grp) {
+        mbar_arrive_expect_tx(&mbar[b], (uint32_t)(W2 * C::RPB * 8));
+        for (int k0 = 0; k0 < W2; k0 += C::BOXK)
+            tma_load_2d(qbase + b * C::QB + k0 * C::RPB, &qmap, grp * C::RPB, k0, &mbar[b]);
+    };
+
+    int grp = blockIdx.x;
+    if (tid == 0 && grp < ngroups) issue(0, grp);
+    for (int it = 0; grp < ngroups; ++it, grp += gridDim.x) {
+        const int b = it & 1;
+        const uint32_t parity = (it >> 1) & 1;
+        const bool more = grp + (int)gridDim.x < ngroups;
+        if (tid == 0 && more) issue(b ^ 1, grp + gridDim.x);
+        const bool ok = mbar_wait_bounded(&mbar[b], parity);
+        if (__syncthreads_or(!ok)) {
+            if (tid == 0) {
+                atomicExch(status, kStatusTimeout);
+                if (more) mbar_wait_bounded(&mbar[b ^ 1], ((it + 1) >> 1) & 1);
             }
-            const float2 B = ws[(size_t)(W2 - k) * H + y];
-            const float2 E2 = c_make(A.x + B.x, A.y - B.y);  // A + conj B
-            const float2 D = c_make(A.x - B.x, A.y + B.y);   // A - conj B
-            const float2 P = c_mul_conj(D, __ldg(twW + k));   // w^-k D
-            const float2 iP = c_mul_i(P);
-            zb[spad(k)] = c_add(E2, iP);
-            if (2 * k != W2) zb[spad(W2 - k)] = c_conj(c_sub(E2, iP));
+            return;
         }
-        __syncthreads();
 
+        // Stage 0 reads with the split pre-pass fused in: element k of row g.
+        const float2* qt = qbase + b * C::QB + g;
         float2 v[I::MAXE];
-        I::run_smem(v, buf, tw, t);
+#pragma unroll
+        for (int q = 0; q < I::bpt(0); ++q) {
+            const int bb = t + q * C::T;
+            if (I::even(0) || bb < NB0) {
+#pragma unroll
+                for (int r = 0; r < R0; ++r) {
+                    const int k = bb + r * NB0;
+                    const float2 A = qt[k * C::RPB];
+                    const float2 B = qt[((W2 - k) % W2) * C::RPB];
+                    const float2 E2 = c_make(A.x + B.x, A.y - B.y);  // A + conj B
+                    const float2 D = c_make(A.x - B.x, A.y + B.y);   // A - conj B
+                    const float2 P = c_mul_conj(D, __ldg(twW + k));   // w^-k D
+                    float2 z = c_make(E2.x - P.y, E2.y + P.x);         // E2 + i P
+                    if (k == 0) z = c_make(A.x + A.y, A.x - A.y);      // packed (X0, X_W2)
+                    v[q * R0 + r] = z;
+                }
+            }
+        }
+        I::run_regs(v, xbuf, tw, t);
 
-        const int y = y0 + g;
+        const int y = grp * C::RPB + g;
         if (y < out_rows) {
             float* orow = out + (size_t)y * out_pitch;
 #pragma unroll
             for (int q = 0; q < I::bpt(I::S - 1); ++q) {
-                int b = t + q * C::T;
-                if (I::even(I::S - 1) || b < NBL) {
+                const int bb = t + q * C::T;
+                if (I::even(I::S - 1) || bb < NBL) {
 #pragma unroll
                     for (int r = 0; r < RL; ++r) {
-                        const int m = b + r * NBL;
+                        const int m = bb + r * NBL;
                         const float2 z = v[q * RL + r];
                         if (vec_ok) {
                             reinterpret_cast<float2*>(orow)[m] = z;
