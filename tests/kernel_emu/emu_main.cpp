@@ -47,14 +47,43 @@ thread_local size_t emu_smem_bytes = 0;
 thread_local unsigned emu_or_calls = 0;
 std::atomic<int> emu_or_flags[2];
 
-inline void __syncthreads() { emu_barrier->arrive_and_wait(); }
-inline int __syncthreads_or(int pred) {
-    const unsigned slot = emu_or_calls++ & 1u;
-    if (pred) emu_or_flags[slot].store(1);
+// __syncthreads compiles to an .aligned barrier: every thread of a warp must
+// execute the same barrier instruction.  Each arrival records its call site
+// (the return address, distinct per template instantiation and call site);
+// after the barrier every thread checks its warp-mates arrived from the same
+// site, so barriers inside divergent branches abort the run.
+thread_local unsigned emu_bar_calls = 0;
+thread_local std::vector<void*>* emu_sites = nullptr;  // [2][blockDim]
+
+static void emu_check_site(unsigned slot, void* site) {
+    const unsigned n = blockDim.x;
+    const unsigned w0 = threadIdx.x & ~31u;
+    for (unsigned l = w0; l < w0 + 32 && l < n; ++l) {
+        if (emu_sites[slot][l] != site) {
+            std::fprintf(stderr, "divergent barrier: thread %u and %u of warp %u at different "
+                                 "barrier instructions\n", threadIdx.x, l, w0 / 32);
+            std::abort();
+        }
+    }
+}
+__attribute__((noinline)) void __syncthreads() {
+    void* site = __builtin_return_address(0);
+    const unsigned slot = emu_bar_calls++ & 1u;
+    emu_sites[slot][threadIdx.x] = site;
     emu_barrier->arrive_and_wait();
-    const int r = emu_or_flags[slot].load();
+    emu_check_site(slot, site);
+}
+__attribute__((noinline)) int __syncthreads_or(int pred) {
+    void* site = __builtin_return_address(0);
+    const unsigned slot = emu_bar_calls++ & 1u;
+    emu_sites[slot][threadIdx.x] = site;
+    const unsigned oslot = emu_or_calls++ & 1u;
+    if (pred) emu_or_flags[oslot].store(1);
     emu_barrier->arrive_and_wait();
-    if (threadIdx.x == 0) emu_or_flags[slot].store(0);
+    emu_check_site(slot, site);
+    const int r = emu_or_flags[oslot].load();
+    emu_barrier->arrive_and_wait();  // plain barrier: everyone has read the flag
+    if (threadIdx.x == 0) emu_or_flags[oslot].store(0);
     return r;
 }
 inline int atomicExch(int* p, int v) { return __atomic_exchange_n(p, v, __ATOMIC_SEQ_CST); }
@@ -121,6 +150,7 @@ void emu_launch(dim3 grid, int block, size_t smem_bytes, K kernel, A... args) {
     std::vector<float4> store((smem_bytes + 15) / 16 + 8);
     float2* smem = reinterpret_cast<float2*>((reinterpret_cast<uintptr_t>(store.data()) + 127) & ~uintptr_t(127));
     std::barrier<> bar(block);
+    std::vector<void*> sites[2] = {std::vector<void*>(block), std::vector<void*>(block)};
     std::vector<std::thread> threads;
     for (int tid = 0; tid < block; ++tid) {
         threads.emplace_back([&, tid] {
@@ -131,6 +161,8 @@ void emu_launch(dim3 grid, int block, size_t smem_bytes, K kernel, A... args) {
             emu_smem = smem;
             emu_smem_bytes = smem_bytes;
             emu_or_calls = 0;
+            emu_bar_calls = 0;
+            emu_sites = sites;
             for (unsigned by = 0; by < grid.y; ++by) {
                 for (unsigned bx = 0; bx < grid.x; ++bx) {
                     blockIdx.x = bx;

@@ -256,15 +256,16 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
         const float2* rcol = rbase + (b * C::FPB + g) * C::RB;
         const float2* scol = sbase + (b * C::FPB + g) * C::SB;
 
+        // One loader for all three column kinds: the groups of a block may hold
+        // different kinds, and the transform below contains block barriers,
+        // which every thread must reach through the same instructions.
+        const bool take_im = mode == 2, keep_im = mode == 0;
+        auto ld = [&](int i) {
+            const float2 x = i < h ? rcol[i] : c_make(0.f, 0.f);
+            return c_make(take_im ? x.y : x.x, keep_im ? x.y : 0.f);
+        };
         float2 v[F::MAXE];
-        if (mode == 0) {
-            auto ld = [&](int i) { return i < h ? rcol[i] : c_make(0.f, 0.f); };
-            F::template run_loader<NZ>(v, ld, xbuf, twf, t);
-        } else {
-            const float* rf = reinterpret_cast<const float*>(rcol) + (mode == 2 ? 1 : 0);
-            auto ld = [&](int i) { return c_make(i < h ? rf[2 * i] : 0.f, 0.f); };
-            F::template run_loader<NZ>(v, ld, xbuf, twf, t);
-        }
+        F::template run_loader<NZ>(v, ld, xbuf, twf, t);
 
         // Pointwise product with the image spectrum column (cuh:86-111).
 #pragma unroll
