@@ -216,7 +216,7 @@ void run_c2r(const float2* Q, int H, float* out, const float2* tw, int orows, in
                orows, ocols, ocols, &g_status);
 }
 
-#define EMU_SIZES(X) X(64) X(128) X(256) X(120) X(240)
+#define EMU_SIZES(X) X(64) X(128) X(256) X(512) X(120) X(240)
 
 static void col(int H, bool conj, int nz, float2* Q, const float2* R, int rp, const float2* spec,
                 const float2* tw, int h, int W2, int rows, int cap) {

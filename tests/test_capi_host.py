@@ -92,3 +92,11 @@ def test_host_validation_codes():
 def test_missing_library_fails_loudly(tmp_path):
     with pytest.raises(RuntimeError, match="not found"):
         _lib.load(str(tmp_path / "libzipfft_b200.so"))
+
+
+def test_built_library_matches_sources():
+    """A stale libzipfft_b200.so (sources changed since the last build) would
+    make every GPU result describe old code."""
+    from zipfft_b200 import build
+
+    assert build.is_current(), "rebuild with python -m zipfft_b200.build"

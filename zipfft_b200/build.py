@@ -50,6 +50,32 @@ def fft_sizes() -> list[int]:
     return [int(s) for s in re.findall(r"X\((\d+)\)", body)]
 
 
+STAMP_PATH = LIB_PATH + ".stamp"
+
+
+def sources_hash() -> str:
+    """Hash of every input of the library build (sources, headers, flags)."""
+    import hashlib
+
+    files = sorted(glob.glob(os.path.join(CSRC, "*")) + glob.glob(os.path.join(ROOT, "include", "*.h")))
+    hsh = hashlib.sha256()
+    for f in files:
+        hsh.update(os.path.basename(f).encode())
+        with open(f, "rb") as fh:
+            hsh.update(fh.read())
+    hsh.update(" ".join(NVCC_FLAGS).encode())
+    return hsh.hexdigest()
+
+
+def is_current() -> bool:
+    """True if the built library matches the current sources."""
+    try:
+        with open(STAMP_PATH) as fh:
+            return os.path.exists(LIB_PATH) and fh.read().strip() == sources_hash()
+    except OSError:
+        return False
+
+
 def _deps_mtime() -> float:
     files = glob.glob(os.path.join(CSRC, "*")) + glob.glob(os.path.join(ROOT, "include", "*.h"))
     files.append(os.path.abspath(__file__))
@@ -68,7 +94,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
     """Compile (if stale) and return the path of libzipfft_b200.so."""
     os.makedirs(BUILD_DIR, exist_ok=True)
     deps = _deps_mtime()
-    if not force and os.path.exists(LIB_PATH) and os.path.getmtime(LIB_PATH) >= deps:
+    if not force and is_current():
         return LIB_PATH
     cc = nvcc()
     jobs_list = []
@@ -91,6 +117,8 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
     tmp = LIB_PATH + ".tmp"
     subprocess.check_call([cc, *ARCH_FLAGS, "-shared", "-cudart", "static", "-o", tmp, *objs])
     os.replace(tmp, LIB_PATH)
+    with open(STAMP_PATH, "w") as fh:
+        fh.write(sources_hash() + "\n")
     if verbose:
         print("linked", os.path.relpath(LIB_PATH, ROOT))
     return LIB_PATH
@@ -100,7 +128,13 @@ def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--jobs", type=int, default=None)
+    ap.add_argument("--check", action="store_true",
+                    help="only report whether the built library matches the sources (exit 1 if not)")
     a = ap.parse_args(argv)
+    if a.check:
+        ok = is_current()
+        print("libzipfft_b200.so is " + ("current" if ok else "STALE: rebuild with python -m zipfft_b200.build"))
+        return 0 if ok else 1
     build(force=a.force, jobs=a.jobs, verbose=True)
     return 0
 

@@ -11,6 +11,7 @@
 //     (cuh:243-259) happen once per device.
 #include <cmath>
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -40,6 +41,33 @@ int fail(int code, const char* fmt, ...) {
     va_end(ap);
     g_last_error = buf;
     return code;
+}
+
+// ZFFT_TRACE=1: print every step of a call to stderr and synchronize after
+// each kernel launch (debugging aid, like CUDA_LAUNCH_BLOCKING).
+bool trace_on() {
+    static const bool on = [] {
+        const char* v = std::getenv("ZFFT_TRACE");
+        return v && v[0] && v[0] != '0';
+    }();
+    return on;
+}
+void trace(const char* fmt, ...) {
+    if (!trace_on()) return;
+    va_list ap;
+    va_start(ap, fmt);
+    std::fprintf(stderr, "[zfft] ");
+    std::vfprintf(stderr, fmt, ap);
+    std::fprintf(stderr, "\n");
+    std::fflush(stderr);
+    va_end(ap);
+}
+cudaError_t trace_sync(cudaStream_t s, const char* what, int t) {
+    if (!trace_on()) return cudaSuccess;
+    trace("launched %s (template %d); synchronizing", what, t);
+    cudaError_t e = cudaStreamSynchronize(s);
+    trace("%s (template %d) done: %s", what, t, cudaGetErrorString(e));
+    return e;
 }
 
 int cuda_fail(cudaError_t e, const char* what) {
@@ -273,10 +301,13 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
     if (device < 0 || device >= ndev || device >= kMaxDevices)
         return fail(ZFFT_ERROR_INVALID_VALUE, "invalid device index %d (%d devices)", device, ndev);
 
+    trace("call: batch %d signal (%d, %d) fft (%d, %d) out (%d, %d) conj %d device %d", batch,
+          sy, sx, H, W, oy, ox, conj ? 1 : 0, device);
     DeviceGuard guard(device);
     if (guard.err != cudaSuccess) return cuda_fail(guard.err, "cudaSetDevice");
     int rc = ensure_device(device);
     if (rc != ZFFT_SUCCESS) return rc;
+    trace("device %d ready", device);
 
     const float2* pool = g_dev_pool[device];
     int* status = g_dev_status[device];
@@ -309,6 +340,7 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
     CUtensorMap qmap;
     e = qmap_fn(W)(Q, H, &qmap);
     if (e != cudaSuccess) return cuda_fail(e, "encoding the intermediate's tensor map");
+    trace("tensor map encoded; chunk %d", chunk);
     ColFn col = col_fn(H);
     R2cFn r2c = r2c_fn(W);
     C2rFn c2r = c2r_fn(W);
@@ -324,6 +356,7 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
                     scale, nz_row, device, s);
             if (e != cudaSuccess) return cuda_fail(e, "row r2c launch");
             timer_close(0, m, s);
+            if ((e = trace_sync(s, "k_row_r2c chunk", t0)) != cudaSuccess) return cuda_fail(e, "k_row_r2c");
         }
         for (int j = 0; j < n; ++j) {
             const int t = t0 + j;
@@ -337,15 +370,18 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
                 e = r2c(input + (size_t)t * sy * sx, Q, twW, sy, sx, H, 0, 1, scale, nz_row, device, s);
                 if (e != cudaSuccess) return cuda_fail(e, "row r2c launch");
                 timer_close(0, m, s);
+                if ((e = trace_sync(s, "k_row_r2c", t)) != cudaSuccess) return cuda_fail(e, "k_row_r2c");
             }
             m = timer_mark(s);
             e = col(Q, Rt, r_pitch, spec, twH, sy, W2, oy, conj, nz_col, status, device, s);
             if (e != cudaSuccess) return cuda_fail(e, "column launch");
             timer_close(1, m, s);
+            if ((e = trace_sync(s, "k_col_fused", t)) != cudaSuccess) return cuda_fail(e, "k_col_fused");
             m = timer_mark(s);
             e = c2r(&qmap, output + (size_t)t * oy * ox, twW, oy, ox, ox, status, device, s);
             if (e != cudaSuccess) return cuda_fail(e, "row c2r launch");
             timer_close(2, m, s);
+            if ((e = trace_sync(s, "k_row_c2r", t)) != cudaSuccess) return cuda_fail(e, "k_row_c2r");
         }
     }
     return ZFFT_SUCCESS;
@@ -511,8 +547,11 @@ int zfft_selftest_wait_timeout(int device, void* stream) {
     int rc = ensure_device(device);
     if (rc != ZFFT_SUCCESS) return rc;
     // ~1 ms at 2 GHz
+    trace("self-test launch");
     e = zf::launch_wait_selftest(g_dev_status[device], 2000000LL, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "self-test launch");
+    if ((e = trace_sync(static_cast<cudaStream_t>(stream), "k_wait_selftest", 0)) != cudaSuccess)
+        return cuda_fail(e, "k_wait_selftest");
     return ZFFT_SUCCESS;
 }
 
