@@ -133,6 +133,13 @@ bool zf::emu_mbar_try_wait(uint64_t* bar, uint32_t parity) {
     std::lock_guard<std::mutex> l(emu_bar_mu);
     return emu_bars.at(bar).phase != parity;  // the phase with that parity completed
 }
+// discard.global.L2 rule: whole 128-byte lines only.
+void zf::emu_discard_line(const void* p) {
+    if (reinterpret_cast<uintptr_t>(p) % 128) {
+        std::fprintf(stderr, "misaligned L2 discard %p\n", p);
+        std::abort();
+    }
+}
 // TMA rules: 16-byte aligned addresses and sizes, destination inside the
 // block's shared memory.
 void zf::emu_check_copy(const void* dst, const void* src, uint32_t bytes) {
@@ -194,7 +201,7 @@ void run_col(float2* Q, const float2* R, int r_pitch, const float2* spec, const 
     int grid = (W2 + 1 + C::FPB - 1) / C::FPB;
     if (grid > cap) grid = cap;
     emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_col_fused<H, CONJ, NZ>, Q, R,
-               r_pitch, spec, tw, h, W2, rows, &g_status);
+               r_pitch, spec, tw, h, W2, rows, R != Q ? 1 : 0, &g_status);
 }
 template <int W2, int NZ>
 void run_r2c(const float* tm, float2* R, const float2* tw, int h, int w, int r_pitch,

@@ -65,7 +65,26 @@ ZF_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// L2 eviction-priority policies for cache-hinted accesses.
+ZF_DEV uint64_t l2_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+ZF_DEV uint64_t l2_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
 // 1D bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned).
+ZF_DEV void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
 ZF_DEV void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
@@ -76,12 +95,29 @@ ZF_DEV void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* ba
 
 // 2D tile load of the tensor map's box at (x, y); x * element size must be a
 // multiple of 16 bytes.
-ZF_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+ZF_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                        uint64_t pol) {
     asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-        "[%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(pol)
         : "memory");
+}
+
+// 8-byte store with an L2 eviction policy.
+ZF_DEV void st_hint(float2* p, float2 v, uint64_t pol) {
+    asm volatile("st.global.L2::cache_hint.v2.f32 [%0], {%1, %2}, %3;" ::"l"(p), "f"(v.x),
+                 "f"(v.y), "l"(pol)
+                 : "memory");
+}
+ZF_DEV void st_hint(float* p, float v, uint64_t pol) {
+    asm volatile("st.global.L2::cache_hint.f32 [%0], %1, %2;" ::"l"(p), "f"(v), "l"(pol) : "memory");
+}
+
+// Drop a 128-byte L2 line without writing it back (its data becomes
+// undefined).  `p` must be 128-byte aligned and no one may read the line again.
+ZF_DEV void l2_discard_line(const void* p) {
+    asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory");
 }
 
 ZF_DEV long long cycle_clock() { return clock64(); }
@@ -109,12 +145,19 @@ inline void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
 }
 inline bool mbar_try_wait(uint64_t* bar, uint32_t parity) { return emu_mbar_try_wait(bar, parity); }
 void emu_check_copy(const void* dst, const void* src, uint32_t bytes);
-inline void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+inline uint64_t l2_evict_first() { return 1; }
+inline uint64_t l2_evict_last() { return 2; }
+inline void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t = 0) {
     emu_check_copy(dst, src, bytes);
     std::memcpy(dst, src, bytes);
     emu_mbar_complete_tx(bar, bytes);
 }
-inline void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+inline void st_hint(float2* p, float2 v, uint64_t) { *p = v; }
+inline void st_hint(float* p, float v, uint64_t) { *p = v; }
+void emu_discard_line(const void* p);
+inline void l2_discard_line(const void* p) { emu_discard_line(p); }
+inline void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                        uint64_t = 0) {
     unsigned char* d = static_cast<unsigned char*>(dst);
     const int row = map->box0 * map->elem;
     for (int j = 0; j < map->box1; ++j) {

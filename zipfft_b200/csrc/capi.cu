@@ -184,7 +184,7 @@ void timer_close(int stage, int start, cudaStream_t s) {
 }
 
 using ColFn = cudaError_t (*)(float2*, const float2*, int, const float2*, const float2*, int, int,
-                              int, bool, int, int*, int, cudaStream_t);
+                              int, bool, int, bool, int*, int, cudaStream_t);
 using R2cFn = cudaError_t (*)(const float*, float2*, const float2*, int, int, int, long long, int,
                               float, int, int, cudaStream_t);
 using QmapFn = cudaError_t (*)(const float2*, int, CUtensorMap*);
@@ -373,7 +373,7 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
                 if ((e = trace_sync(s, "k_row_r2c", t)) != cudaSuccess) return cuda_fail(e, "k_row_r2c");
             }
             m = timer_mark(s);
-            e = col(Q, Rt, r_pitch, spec, twH, sy, W2, oy, conj, nz_col, status, device, s);
+            e = col(Q, Rt, r_pitch, spec, twH, sy, W2, oy, conj, nz_col, chunk > 0, status, device, s);
             if (e != cudaSuccess) return cuda_fail(e, "column launch");
             timer_close(1, m, s);
             if ((e = trace_sync(s, "k_col_fused", t)) != cudaSuccess) return cuda_fail(e, "k_col_fused");

@@ -19,6 +19,8 @@
 // the host in double precision and rounded once to float.
 #pragma once
 
+#include <type_traits>
+
 #if defined(__CUDACC__)
 #include <cuda_runtime.h>
 #define ZF_HD __host__ __device__ __forceinline__
@@ -132,6 +134,15 @@ ZF_HD float2 c_mul_w(float2 a) {
         constexpr float wr = float(cx_cos2pi(m, N));
         constexpr float wi = float(-cx_sin2pi(m, N));
         return c_mul(a, c_make(wr, wi));
+    }
+}
+
+// Calls f(std::integral_constant<int, I>) for I = 0 .. N-1 (compile-time index).
+template <int N, int I = 0, class F>
+ZF_HD void static_for(F&& f) {
+    if constexpr (I < N) {
+        f(std::integral_constant<int, I>{});
+        static_for<N, I + 1>(f);
     }
 }
 

@@ -68,7 +68,8 @@ cudaError_t r2c_t(const float* tmpl, float2* R, const float2* tw, int h, int w, 
 
 template <int H, bool CONJ, int NZ>
 cudaError_t col_t(float2* Q, const float2* R, int r_pitch, const float2* spec, const float2* tw,
-                  int h, int W2, int store_rows, int* status, int device, cudaStream_t s) {
+                  int h, int W2, int store_rows, bool discard_r, int* status, int device,
+                  cudaStream_t s) {
     using C = ColCfg<H, NZ>;
     static KernelState st;
     auto kernel = k_col_fused<H, CONJ, NZ>;
@@ -76,7 +77,8 @@ cudaError_t col_t(float2* Q, const float2* R, int r_pitch, const float2* spec, c
     cudaError_t e = configure(kernel, st, C::SMEM, C::THREADS, device, &cap);
     if (e != cudaSuccess) return e;
     const int grid = min_int((W2 + 1 + C::FPB - 1) / C::FPB, cap);
-    kernel<<<grid, C::THREADS, C::SMEM, s>>>(Q, R, r_pitch, spec, tw, h, W2, store_rows, status);
+    kernel<<<grid, C::THREADS, C::SMEM, s>>>(Q, R, r_pitch, spec, tw, h, W2, store_rows,
+                                             discard_r ? 1 : 0, status);
     return cudaGetLastError();
 }
 
@@ -118,10 +120,11 @@ cudaError_t ZF_CAT(launch_row_r2c_, ZF_SIZE)(const float* tmpl, float2* R, const
 
 cudaError_t ZF_CAT(launch_col_, ZF_SIZE)(float2* Q, const float2* R, int r_pitch,
                                          const float2* spec, const float2* tw, int h, int W2,
-                                         int store_rows, bool conj, int nz, int* status,
-                                         int device, cudaStream_t s) {
+                                         int store_rows, bool conj, int nz, bool discard_r,
+                                         int* status, int device, cudaStream_t s) {
     constexpr int H = ZF_SIZE;
-#define ZF_COL(CJ, NZV) col_t<H, CJ, NZV>(Q, R, r_pitch, spec, tw, h, W2, store_rows, status, device, s)
+#define ZF_COL(CJ, NZV) \
+    col_t<H, CJ, NZV>(Q, R, r_pitch, spec, tw, h, W2, store_rows, discard_r, status, device, s)
     if constexpr (kPruned) {
         if (nz == 1) return conj ? ZF_COL(true, 1) : ZF_COL(false, 1);
         if (nz == 2) return conj ? ZF_COL(true, 2) : ZF_COL(false, 2);

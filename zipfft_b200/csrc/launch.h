@@ -23,7 +23,7 @@ namespace zf {
                                    int nz, int device, cudaStream_t s);                          \
     cudaError_t launch_col_##N(float2* Q, const float2* R, int r_pitch, const float2* spec,      \
                                const float2* tw, int h, int W2, int store_rows, bool conj, int nz, \
-                               int* status, int device, cudaStream_t s);                         \
+                               bool discard_r, int* status, int device, cudaStream_t s);         \
     cudaError_t make_qmap_##N(const float2* Q, int H, CUtensorMap* map);                        \
     cudaError_t launch_row_c2r_##N(const CUtensorMap* qmap, float* out, const float2* tw,        \
                                    int out_rows, int out_cols, int out_pitch, int* status,       \

@@ -108,7 +108,10 @@ __global__ void __launch_bounds__(R2cCfg<W2>::THREADS)
     typename F::Twiddles tw;
     F::template load_twiddles<2 * W2>(tw, twW, t);
 
-    for (int n0 = blockIdx.x * C::RPB; n0 < h; n0 += gridDim.x * C::RPB) {
+    // Row groups cover rows [0, round_up(h, 2)): the padding row of an odd h
+    // is written as zeros by the split pass below.
+    const int h_pad = (h + 1) & ~1;
+    for (int n0 = blockIdx.x * C::RPB; n0 < h_pad; n0 += gridDim.x * C::RPB) {
         const int n = n0 + g;
         RowLoader ld{tm + (size_t)(n < h ? n : 0) * w, n < h ? w : 0};
         float2 v[F::MAXE];
@@ -132,7 +135,15 @@ __global__ void __launch_bounds__(R2cCfg<W2>::THREADS)
         for (int it = tid; it < NIT; it += C::THREADS) {
             const int nl = it % C::RPB, k = it / C::RPB;
             const int nn = n0 + nl;
-            if (nn >= h) continue;
+            if (nn >= h) {
+                // Row h of an odd-height template is the zero padding that
+                // the column kernel's 16-byte copies also fetch.
+                if (nn == h && (h & 1)) {
+                    Rt[(size_t)k * r_pitch + nn] = c_make(0.f, 0.f);
+                    if (k != 0 && 2 * k != W2) Rt[(size_t)(W2 - k) * r_pitch + nn] = c_make(0.f, 0.f);
+                }
+                continue;
+            }
             const float2* zb = smem + nl * C::XB;
             const float2 A = zb[spad(k)];
             if (k == 0) {
@@ -180,7 +191,7 @@ template <int H, bool CONJ, int NZ>
 __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
     k_col_fused(float2* __restrict__ Q, const float2* __restrict__ R, int r_pitch,
                 const float2* __restrict__ spec, const float2* __restrict__ twH, int h, int W2,
-                int store_rows, int* __restrict__ status) {
+                int store_rows, int discard_r, int* __restrict__ status) {
     using C = ColCfg<H, NZ>;
     using F = Stockham<H, C::T, false, false>;
     using I = Stockham<H, C::T, true, true>;
@@ -216,6 +227,11 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
 
     const uint32_t r_bytes = (uint32_t)round_up(h, 2) * 8u;
     const int stride = gridDim.x * C::FPB;
+    // L2 policy: the spectrum and template columns stream through (each is
+    // read once per template); the intermediate Q is kept resident for the
+    // row kernel that reads it next.
+    const uint64_t pol_stream = l2_evict_first();
+    const uint64_t pol_keep = l2_evict_last();
 
     // Thread 0 fetches the spectrum and template columns of group vc0 into buffer b.
     auto issue = [&](int b, int vc0) {
@@ -226,10 +242,11 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
         for (int j = 0; j < C::FPB; ++j) {
             const int vc = vc0 + j;
             if (vc > W2) break;
-            tma_load_1d(sbase + (b * C::FPB + j) * C::SB, spec + (size_t)vc * H, H * 8u, &mbar[b]);
+            tma_load_1d(sbase + (b * C::FPB + j) * C::SB, spec + (size_t)vc * H, H * 8u, &mbar[b],
+                        pol_stream);
             const int rc = vc == W2 ? 0 : vc;
             tma_load_1d(rbase + (b * C::FPB + j) * C::RB, R + (size_t)rc * r_pitch, r_bytes,
-                        &mbar[b]);
+                        &mbar[b], pol_stream);
         }
     };
 
@@ -255,17 +272,43 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
         const int mode = vc == 0 ? 1 : (vc == W2 ? 2 : 0);
         const float2* rcol = rbase + (b * C::FPB + g) * C::RB;
         const float2* scol = sbase + (b * C::FPB + g) * C::SB;
+        // A template column outside Q (the chunked layout) has no other reader
+        // once copied: drop its whole 128-byte lines from L2 without write-back.
+        // Packed column 0 is read by two column kinds and is kept.
+        if (discard_r && active && mode == 0) {
+            const char* c0 = reinterpret_cast<const char*>(R + (size_t)vc * r_pitch);
+            const size_t lo = (reinterpret_cast<size_t>(c0) + 127) & ~size_t(127);
+            const size_t hi = (reinterpret_cast<size_t>(c0) + r_bytes) & ~size_t(127);
+            for (size_t a = lo + (size_t)t * 128; a < hi; a += (size_t)C::T * 128)
+                l2_discard_line(reinterpret_cast<const void*>(a));
+        }
 
-        // One loader for all three column kinds: the groups of a block may hold
-        // different kinds, and the transform below contains block barriers,
-        // which every thread must reach through the same instructions.
-        const bool take_im = mode == 2, keep_im = mode == 0;
-        auto ld = [&](int i) {
-            const float2 x = i < h ? rcol[i] : c_make(0.f, 0.f);
-            return c_make(take_im ? x.y : x.x, keep_im ? x.y : 0.f);
-        };
+        // The template buffer is zero past h (zero fill beyond the copied
+        // length; the row kernel writes the padding row of an odd h), so the
+        // loader reads it unconditionally.
         float2 v[F::MAXE];
-        F::template run_loader<NZ>(v, ld, xbuf, twf, t);
+        if constexpr (C::FPB == 1) {
+            // The column kind is uniform across the block: branching on it
+            // keeps the block barriers inside the transform convergent.
+            if (mode == 0) {
+                auto ld = [&](int i) { return rcol[i]; };
+                F::template run_loader<NZ>(v, ld, xbuf, twf, t);
+            } else {
+                const float* rf = reinterpret_cast<const float*>(rcol) + (mode == 2 ? 1 : 0);
+                auto ld = [&](int i) { return c_make(rf[2 * i], 0.f); };
+                F::template run_loader<NZ>(v, ld, xbuf, twf, t);
+            }
+        } else {
+            // Groups of one block may hold different column kinds: one loader
+            // with per-element selects, so every thread reaches the block
+            // barriers inside the transform through the same instructions.
+            const bool take_im = mode == 2, keep_im = mode == 0;
+            auto ld = [&](int i) {
+                const float2 x = rcol[i];
+                return c_make(take_im ? x.y : x.x, keep_im ? x.y : 0.f);
+            };
+            F::template run_loader<NZ>(v, ld, xbuf, twf, t);
+        }
 
         // Pointwise product with the image spectrum column (cuh:86-111).
 #pragma unroll
@@ -299,7 +342,7 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
 #pragma unroll
                         for (int r = 0; r < RO; ++r) {
                             const int y = bb + r * NBO;
-                            if (full || y < store_rows) dst[y] = v[q * RO + r];
+                            if (full || y < store_rows) st_hint(dst + y, v[q * RO + r], pol_keep);
                         }
                     }
                 }
@@ -312,7 +355,7 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
 #pragma unroll
                         for (int r = 0; r < RO; ++r) {
                             const int y = bb + r * NBO;
-                            if (full || y < store_rows) dstf[2 * y] = v[q * RO + r].x;
+                            if (full || y < store_rows) st_hint(dstf + 2 * y, v[q * RO + r].x, pol_keep);
                         }
                     }
                 }
@@ -342,7 +385,10 @@ struct C2rCfg {
     static constexpr int RPB = cmax(2, 128 / T);  // rows per block (even: TMA x alignment)
     static constexpr int THREADS = RPB * T;
     static constexpr int MINB = cmax(1, 512 / THREADS);
-    static constexpr int XB = xbuf_len(W2);
+    // Rows are interleaved across lanes (row = tid % RPB): the tile reads of
+    // the pre-pass are then contiguous across a warp.  With two rows, row
+    // buffers 16 banks apart keep the stage exchanges conflict free.
+    static constexpr int XB = RPB == 2 ? round_up(spad_size(W2) - 8, 16) + 8 : xbuf_len(W2);
     static constexpr int BOXK = tma_box(W2);
     static constexpr int QB = round_up(W2 * RPB, 16);  // one Q tile
     static constexpr int FLOATS = 2 * QB + RPB * XB;
@@ -362,7 +408,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     static_assert((C::RPB * 8) % 16 == 0, "TMA inner box must be a multiple of 16 bytes");
 
     const int tid = threadIdx.x;
-    const int g = tid / C::T, t = tid % C::T;
+    const int g = tid % C::RPB, t = tid / C::RPB;
     float2* smem = dyn_smem();
     float2* qbase = smem;                       // [2][W2][RPB]
     float2* xbuf = smem + 2 * C::QB + g * C::XB;
@@ -377,15 +423,28 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
 
     typename I::Twiddles tw;
     I::template load_twiddles<2 * W2>(tw, twW, t);
+    // Pre-pass twiddles w_W^-k for k = bb + r NB0: w^-bb (per butterfly, from
+    // the table) times w_W^-(r NB0) = w_{2 R0}^-r (compile-time roots).
+    float2 wpre[I::bpt(0)];
+#pragma unroll
+    for (int q = 0; q < I::bpt(0); ++q) {
+        const int bb = t + q * C::T;
+        wpre[q] = (I::even(0) || bb < NB0) ? c_conj(__ldg(twW + bb)) : c_make(1.f, 0.f);
+    }
 
     const bool vec_ok = out_cols == 2 * W2 && (out_pitch % 2) == 0 &&
                         (reinterpret_cast<size_t>(out) % 8) == 0;
     const int ngroups = (out_rows + C::RPB - 1) / C::RPB;
 
+    // L2 policy: Q lines stay resident (the next template's column pass
+    // overwrites them there without a DRAM round trip); output rows stream out.
+    const uint64_t pol_keep = l2_evict_last();
+    const uint64_t pol_stream = l2_evict_first();
     auto issue = [&](int b, int grp) {
         mbar_arrive_expect_tx(&mbar[b], (uint32_t)(W2 * C::RPB * 8));
         for (int k0 = 0; k0 < W2; k0 += C::BOXK)
-            tma_load_2d(qbase + b * C::QB + k0 * C::RPB, &qmap, grp * C::RPB, k0, &mbar[b]);
+            tma_load_2d(qbase + b * C::QB + k0 * C::RPB, &qmap, grp * C::RPB, k0, &mbar[b],
+                        pol_keep);
     };
 
     int grp = blockIdx.x;
@@ -411,18 +470,20 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
         for (int q = 0; q < I::bpt(0); ++q) {
             const int bb = t + q * C::T;
             if (I::even(0) || bb < NB0) {
-#pragma unroll
-                for (int r = 0; r < R0; ++r) {
+                const float2 wb = wpre[q];
+                static_for<R0>([&](auto rc) {
+                    constexpr int r = decltype(rc)::value;
                     const int k = bb + r * NB0;
                     const float2 A = qt[k * C::RPB];
                     const float2 B = qt[((W2 - k) % W2) * C::RPB];
                     const float2 E2 = c_make(A.x + B.x, A.y - B.y);  // A + conj B
                     const float2 D = c_make(A.x - B.x, A.y + B.y);   // A - conj B
-                    const float2 P = c_mul_conj(D, __ldg(twW + k));   // w^-k D
+                    // w^-k D = (w^-bb D) w_{2 R0}^-r
+                    const float2 P = c_mul_w<2 * R0 - r, 2 * R0, false>(c_mul(D, wb));
                     float2 z = c_make(E2.x - P.y, E2.y + P.x);         // E2 + i P
-                    if (k == 0) z = c_make(A.x + A.y, A.x - A.y);      // packed (X0, X_W2)
+                    if (r == 0 && bb == 0) z = c_make(A.x + A.y, A.x - A.y);  // packed (X0, X_W2)
                     v[q * R0 + r] = z;
-                }
+                });
             }
         }
         I::run_regs(v, xbuf, tw, t);
@@ -439,10 +500,10 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                         const int m = bb + r * NBL;
                         const float2 z = v[q * RL + r];
                         if (vec_ok) {
-                            reinterpret_cast<float2*>(orow)[m] = z;
+                            st_hint(reinterpret_cast<float2*>(orow) + m, z, pol_stream);
                         } else {
-                            if (2 * m < out_cols) orow[2 * m] = z.x;
-                            if (2 * m + 1 < out_cols) orow[2 * m + 1] = z.y;
+                            if (2 * m < out_cols) st_hint(orow + 2 * m, z.x, pol_stream);
+                            if (2 * m + 1 < out_cols) st_hint(orow + 2 * m + 1, z.y, pol_stream);
                         }
                     }
                 }
