@@ -71,6 +71,26 @@ ZFFT_API int zfft_padded_real_conv_2d(const float* input, int batch, int signal_
                              const void* conv_data, float* output, int output_y, int output_x,
                              int fft_size_y, int fft_size_x, int device, void* stream);
 
+/* Cross-correlation exactly as zfft_padded_real_corr_2d, for callers that
+ * cannot allocate device memory.  No counterpart in the reference (whose
+ * binding takes a caller-allocated workspace tensor).  Instead of a workspace
+ * argument it uses a fixed 16 MiB scratch array that lives in the library's
+ * own device memory: every GPU that loads the library holds it until the
+ * process exits.  Limit: fft_y * (fft_x / 2) complex values must fit, i.e.
+ * fft_y * fft_x <= 4,194,304 (e.g. 2048 x 2048, 4096 x 1024); larger sizes
+ * return ZFFT_ERROR_INVALID_VALUE with an explanation.  The call itself makes
+ * no cudaMalloc / cudaFree or other allocating call.  The first call on a
+ * device looks the array's device address up (and uploads the twiddle tables,
+ * as every first call does); make that first call before any stream capture.
+ * All calls share the one array and it keeps the previous call's contents
+ * (nothing in it needs to start at zero): calls that can overlap on the GPU
+ * (different streams, or different host threads without ordering) race on it
+ * and give wrong results; serialize them. */
+ZFFT_API int zfft_padded_real_corr_2d_noalloc(const float* input, int batch, int signal_y,
+                                              int signal_x, const void* conv_data, float* output,
+                                              int output_y, int output_x, int fft_size_y,
+                                              int fft_size_x, int device, void* stream);
+
 /* Bytes of fft_workspace the two calls above need for an (fft_y, fft_x)
  * image: fft_y * (fft_x / 2) complex64 values, independent of the batch
  * (templates are processed one after another through the same slice).

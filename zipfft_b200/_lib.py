@@ -26,6 +26,8 @@ _CONV_ARGS = [_vp, _c_int, _c_int, _c_int, _vp, _c_size, _vp, _vp, _c_int, _c_in
 SIGNATURES = {
     "zfft_padded_real_corr_2d": (_c_int, _CONV_ARGS),
     "zfft_padded_real_conv_2d": (_c_int, _CONV_ARGS),
+    "zfft_padded_real_corr_2d_noalloc": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _c_int,
+                                                  _c_int, _c_int, _c_int, _c_int, _vp]),
     "zfft_workspace_bytes": (_c_size, [_c_int, _c_int]),
     "zfft_is_fft_size_supported": (_c_int, [_c_int]),
     "zfft_get_supported_conv_configs": (_c_int, [ctypes.POINTER(ctypes.c_int), _c_int]),

@@ -96,6 +96,14 @@ int tw_offset(int n) {
     return -1;
 }
 
+// Scratch of zfft_padded_real_corr_2d_noalloc: a fixed 16 MiB array in the
+// library's own device memory (one per GPU that loads the library, held until
+// the process exits), so that entry point never allocates.  Host code must
+// not use g_noalloc_ws as a pointer: it is a host-side stand-in for the
+// symbol; the device address comes from cudaGetSymbolAddress.
+constexpr size_t kNoAllocBytes = size_t(16) << 20;
+__device__ __align__(256) float2 g_noalloc_ws[kNoAllocBytes / sizeof(float2)];
+
 std::mutex g_init_mu;
 bool g_dev_ready[kMaxDevices];
 float2* g_dev_pool[kMaxDevices];
@@ -506,6 +514,48 @@ int zfft_stage_timing_read(double* ms, int* launches, int n) {
 }
 
 int zfft_get_version(void) { return kVersion; }
+
+int zfft_padded_real_corr_2d_noalloc(const float* input, int batch, int signal_y, int signal_x,
+                                     const void* conv_data, float* output, int output_y,
+                                     int output_x, int fft_size_y, int fft_size_x, int device,
+                                     void* stream) {
+    g_last_error.clear();
+    const size_t need = zfft_workspace_bytes(fft_size_y, fft_size_x);
+    if (need == 0)
+        return fail(ZFFT_ERROR_UNSUPPORTED,
+                    "Unsupported padded convolution configuration: fft_y=%d, fft_x=%d",
+                    fft_size_y, fft_size_x);
+    if (need > kNoAllocBytes)
+        return fail(ZFFT_ERROR_INVALID_VALUE,
+                    "fft size (%d, %d) needs %zu bytes of scratch; the allocation-free entry "
+                    "point has a fixed %zu-byte scratch array (fft_y * fft_x / 2 <= %zu); use "
+                    "zfft_padded_real_corr_2d with a caller-provided workspace",
+                    fft_size_y, fft_size_x, need, kNoAllocBytes, kNoAllocBytes / sizeof(float2));
+    int ndev = 0;
+    cudaError_t e = cudaGetDeviceCount(&ndev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+    if (device < 0 || device >= ndev || device >= kMaxDevices)
+        return fail(ZFFT_ERROR_INVALID_VALUE, "invalid device index %d (%d devices)", device, ndev);
+    // Set-up once per device, with that device current: the array's device
+    // address (the symbol itself is only a host-side stand-in).
+    static std::mutex mu;
+    static float2* scratch[kMaxDevices];
+    float2* ws = nullptr;
+    {
+        DeviceGuard guard(device);
+        if (guard.err != cudaSuccess) return cuda_fail(guard.err, "cudaSetDevice");
+        std::lock_guard<std::mutex> lock(mu);
+        if (!scratch[device]) {
+            void* p = nullptr;
+            e = cudaGetSymbolAddress(&p, g_noalloc_ws);
+            if (e != cudaSuccess) return cuda_fail(e, "resolving the fixed scratch array");
+            scratch[device] = static_cast<float2*>(p);
+        }
+        ws = scratch[device];
+    }
+    return run(input, batch, signal_y, signal_x, ws, kNoAllocBytes, conv_data, output, output_y,
+               output_x, fft_size_y, fft_size_x, true, device, stream);
+}
 
 int zfft_check_device_status(int device, void* stream, int* status) {
     g_last_error.clear();
