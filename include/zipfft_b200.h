@@ -71,6 +71,34 @@ ZFFT_API int zfft_padded_real_conv_2d(const float* input, int batch, int signal_
                              const void* conv_data, float* output, int output_y, int output_x,
                              int fft_size_y, int fft_size_x, int device, void* stream);
 
+/* 2D template matching's per-pixel search: cross-correlate every template
+ * as zfft_padded_real_corr_2d does, but instead of writing one map per
+ * template fold each correlation into running maps: max_map[y][x] keeps the
+ * largest correlation seen and arg_map[y][x] the index of the template that
+ * produced it (template t of this call has index template_index_base + t;
+ * on ties the lower index is kept, since templates are folded in increasing
+ * index order and only strictly larger values replace the maximum).  Both
+ * maps are output_y x output_x (valid crop or full, as for corr).  reset != 0:
+ * the call's first template overwrites the maps instead of comparing, so
+ * they need no initialisation.  No counterpart in the reference (the fused
+ * max / argmax of 2D template matching that its README motivates). */
+ZFFT_API int zfft_padded_real_corr_2d_max(const float* input, int batch, int signal_y,
+                                          int signal_x, void* fft_workspace,
+                                          size_t fft_workspace_bytes, const void* conv_data,
+                                          float* max_map, int32_t* arg_map, int output_y,
+                                          int output_x, int fft_size_y, int fft_size_x,
+                                          int template_index_base, int reset, int device,
+                                          void* stream);
+
+/* (max, argmax) pairs <-> one int64 key each, ordered so that a single
+ * integer MAX reduction across GPUs (e.g. ncclAllReduce with ncclInt64 /
+ * ncclMax) yields the global maximum and, on ties, the lowest index.  n
+ * elements; asynchronous on `stream`.  No counterpart in the reference. */
+ZFFT_API int zfft_pack_max_arg(const float* max_map, const int32_t* arg_map, int64_t* keys,
+                               size_t n, int device, void* stream);
+ZFFT_API int zfft_unpack_max_arg(const int64_t* keys, float* max_map, int32_t* arg_map, size_t n,
+                                 int device, void* stream);
+
 /* Cross-correlation exactly as zfft_padded_real_corr_2d, for callers that
  * cannot allocate device memory.  No counterpart in the reference (whose
  * binding takes a caller-allocated workspace tensor).  Instead of a workspace

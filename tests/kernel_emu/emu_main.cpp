@@ -9,13 +9,15 @@
 //
 // Usage: zf_emu <in.bin> <out.bin>
 //   in.bin : int32 header {B, sy, sx, H, W, oy, ox, conj, grid_cap, nz_col,
-//            nz_row, chunk}, float32 templates [B][sy][sx], complex64
-//            spectrum [W/2+1][H]
-//   out.bin: float32 [B][oy][ox]
+//            nz_row, chunk, max_mode}, float32 templates [B][sy][sx],
+//            complex64 spectrum [W/2+1][H]
+//   out.bin: float32 [B][oy][ox] maps, or with max_mode the float32 [oy][ox]
+//            running maximum and int32 [oy][ox] argmax over the templates
 #include <atomic>
 #include <barrier>
 #include <cmath>
 #include <map>
+#define INFINITY __builtin_inff()
 #include <mutex>
 #include <cstdio>
 #include <cstdlib>
@@ -27,6 +29,10 @@
 struct float2 {
     float x, y;
 };
+struct __attribute__((aligned(8))) int2 {
+    int x, y;
+};
+inline int2 make_int2(int x, int y) { return int2{x, y}; }
 struct __attribute__((aligned(16))) float4 {
     float x, y, z, w;
 };
@@ -213,14 +219,19 @@ void run_r2c(const float* tm, float2* R, const float2* tw, int h, int w, int r_p
                R, tw, h, w, r_pitch, r_tstride, sc);
 }
 template <int W2>
-void run_c2r(const float2* Q, int H, float* out, const float2* tw, int orows, int ocols, int cap) {
+void run_c2r(const float2* Q, int H, float* out, int* arg, const float2* tw, int orows, int ocols,
+             int tindex, int reset, int cap) {
     using C = zf::C2rCfg<W2>;
     zf::CUtensorMap map{reinterpret_cast<const unsigned char*>(Q), H, W2, (long long)H * 8,
                         C::RPB, C::BOXK, 8};
     int groups = (orows + C::RPB - 1) / C::RPB;
     int grid = groups < cap ? groups : cap;
-    emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_row_c2r<W2>, map, out, tw,
-               orows, ocols, ocols, &g_status);
+    if (arg)
+        emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_row_c2r<W2, zf::kRunningMax>,
+                   map, out, arg, tw, orows, ocols, ocols, tindex, reset, &g_status);
+    else
+        emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_row_c2r<W2, zf::kStoreMap>,
+                   map, out, (int*)nullptr, tw, orows, ocols, ocols, 0, 0, &g_status);
 }
 
 #define EMU_SIZES(X) X(64) X(128) X(256) X(512) X(120) X(240)
@@ -256,10 +267,10 @@ static void r2c(int W, int nz, const float* tm, float2* R, const float2* tw, int
     std::fprintf(stderr, "unsupported W %d\n", W);
     std::exit(2);
 }
-static void c2r(int W, const float2* Q, int H, float* out, const float2* tw, int orows, int ocols,
-                int cap) {
+static void c2r(int W, const float2* Q, int H, float* out, int* arg, const float2* tw, int orows,
+                int ocols, int tindex, int reset, int cap) {
 #define X(N) \
-    if (W == N) return run_c2r<N / 2>(Q, H, out, tw, orows, ocols, cap);
+    if (W == N) return run_c2r<N / 2>(Q, H, out, arg, tw, orows, ocols, tindex, reset, cap);
     EMU_SIZES(X)
 #undef X
     std::fprintf(stderr, "unsupported W %d\n", W);
@@ -273,11 +284,12 @@ int main(int argc, char** argv) {
     }
     FILE* f = std::fopen(argv[1], "rb");
     if (!f) return 2;
-    int hd[12];
-    if (std::fread(hd, sizeof(int), 12, f) != 12) return 2;
+    int hd[13];
+    if (std::fread(hd, sizeof(int), 13, f) != 13) return 2;
     const int B = hd[0], sy = hd[1], sx = hd[2], H = hd[3], W = hd[4], oy = hd[5], ox = hd[6];
     const bool conj = hd[7] != 0;
     const int cap = hd[8], nz_col = hd[9], nz_row = hd[10], chunk = hd[11];
+    const bool max_mode = hd[12] != 0;  // fold into running max / argmax maps
     const int W2 = W / 2;
     std::vector<float> tm((size_t)B * sy * sx);
     std::vector<float2> spec((size_t)(W2 + 1) * H);
@@ -293,7 +305,8 @@ int main(int argc, char** argv) {
     std::vector<float4> ws_store((q_elems + (chunk > 0 ? chunk : 0) * r_elems + 1) / 2 + 1);
     float2* Q = reinterpret_cast<float2*>(ws_store.data());
     float2* Rregion = Q + q_elems;
-    std::vector<float> out((size_t)B * oy * ox);
+    std::vector<float> out((size_t)(max_mode ? 1 : B) * oy * ox);
+    std::vector<int> arg(max_mode ? (size_t)oy * ox : 0);
     auto twH = twiddles(H), twW = twiddles(W);
     const float scale = float(1.0 / (double(H) * double(W)));
     const int step = chunk > 0 ? chunk : 1;
@@ -313,7 +326,10 @@ int main(int argc, char** argv) {
                 r2c(W, nz_row, tm.data() + (size_t)t * sy * sx, Q, twW.data(), sy, sx, H, 0, 1, scale, cap);
             }
             col(H, conj, nz_col, Q, Rt, rp, spec.data(), twH.data(), sy, W2, oy, cap);
-            c2r(W, Q, H, out.data() + (size_t)t * oy * ox, twW.data(), oy, ox, cap);
+            if (max_mode)
+                c2r(W, Q, H, out.data(), arg.data(), twW.data(), oy, ox, t, t == 0, cap);
+            else
+                c2r(W, Q, H, out.data() + (size_t)t * oy * ox, nullptr, twW.data(), oy, ox, 0, 0, cap);
         }
     }
     if (g_status != 0) {
@@ -323,6 +339,7 @@ int main(int argc, char** argv) {
     FILE* g = std::fopen(argv[2], "wb");
     if (!g) return 2;
     std::fwrite(out.data(), sizeof(float), out.size(), g);
+    if (max_mode) std::fwrite(arg.data(), sizeof(int), arg.size(), g);
     std::fclose(g);
     return 0;
 }

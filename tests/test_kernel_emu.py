@@ -46,7 +46,7 @@ def nz_of(n, length):
 
 
 def run_emu(exe, tmp_path, B, sy, sx, H, W, conj, full, nz_col=None, nz_row=None, seed=0,
-            chunk=0):
+            chunk=0, max_mode=False):
     rng = np.random.default_rng(seed)
     img = rng.standard_normal((H, W)).astype(np.float32)
     tm = rng.standard_normal((B, sy, sx)).astype(np.float32)
@@ -56,14 +56,20 @@ def run_emu(exe, tmp_path, B, sy, sx, H, W, conj, full, nz_col=None, nz_row=None
     nz_row = nz_of(W // 2, (sx + 1) // 2) if nz_row is None else nz_row
     fin, fout = str(tmp_path / "in.bin"), str(tmp_path / "out.bin")
     with open(fin, "wb") as f:
-        np.array([B, sy, sx, H, W, oy, ox, int(conj), 3, nz_col, nz_row, chunk],
+        np.array([B, sy, sx, H, W, oy, ox, int(conj), 3, nz_col, nz_row, chunk, int(max_mode)],
                  np.int32).tofile(f)
         tm.tofile(f)
         spec.tofile(f)
     res = subprocess.run([exe, fin, fout], capture_output=True, text=True)
     assert res.returncode == 0, res.stderr[-4000:]
+    ref = O.padded_corr2d_f64(tm, spec, H, W, conj, full)
+    if max_mode:
+        raw = np.fromfile(fout, np.uint8)
+        mx = raw[: oy * ox * 4].view(np.float32).reshape(oy, ox)
+        am = raw[oy * ox * 4:].view(np.int32).reshape(oy, ox)
+        return (mx, am), ref
     out = np.fromfile(fout, np.float32).reshape(B, oy, ox)
-    return out, O.padded_corr2d_f64(tm, spec, H, W, conj, full)
+    return out, ref
 
 
 CASES = [
@@ -92,3 +98,19 @@ def test_emulated_kernels_match_oracle(emu, tmp_path, case):
     out, ref = run_emu(emu, tmp_path, B, sy, sx, H, W, conj, full, nzc, nzr, chunk=chunk)
     assert O.rel_l2(ref, out) < 1e-6
     assert O.max_abs_over_peak(ref, out) < 1e-5
+
+
+@pytest.mark.parametrize("chunk", [0, 2])
+def test_emulated_running_max_argmax(emu, tmp_path, chunk):
+    """The max / argmax epilogue of the inverse row pass."""
+    B, H, W = 5, 64, 128
+    (mx, am), ref = run_emu(emu, tmp_path, B, 12, 9, H, W, True, True, chunk=chunk, max_mode=True)
+    assert np.allclose(mx, ref.max(axis=0), rtol=0, atol=1e-5 * np.abs(ref).max())
+    order = np.sort(ref, axis=0)
+    margin = order[-1] - order[-2]
+    sure = margin > 1e-4 * np.abs(ref).max()
+    assert sure.mean() > 0.99
+    assert np.array_equal(am[sure], ref.argmax(axis=0)[sure])
+    (mv, av), refv = run_emu(emu, tmp_path, B, 12, 9, H, W, True, False, max_mode=True)
+    assert mv.shape == (H - 11, W - 8)
+    assert np.allclose(mv, refv.max(axis=0), rtol=0, atol=1e-5 * np.abs(refv).max())

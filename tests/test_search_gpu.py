@@ -1,0 +1,146 @@
+"""The fused running max / argmax (corr_max), the packed keys, and the
+template search on the GPU, against the oracle."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import xcorr_oracle as O
+from tests.gpu_helpers import make_inputs
+from zipfft_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+
+
+def maps(ref):
+    """Oracle max / argmax over templates and the pixels whose winner is
+    unambiguous (lead over the runner-up above the tolerance)."""
+    order = np.sort(ref, axis=0)
+    sure = (order[-1] - order[-2]) > 1e-4 * np.abs(ref).max()
+    return ref.max(axis=0), ref.argmax(axis=0), sure
+
+
+def run_corr_max(tm, spec, H, W, full, base=0, reset=True, mx=None, am=None, ws=None):
+    import zipfft
+
+    dev = torch.device("cuda", 0)
+    B, h, w = tm.shape
+    oy, ox = O.out_shape(h, w, H, W, full)
+    if mx is None:
+        mx = torch.full((oy, ox), float("nan"), device=dev)
+        am = torch.full((oy, ox), -7, dtype=torch.int32, device=dev)
+    if ws is None:
+        ws = torch.empty((B, H, W // 2 + 1), dtype=torch.complex64, device=dev)
+    zipfft.padded_rconv2d.corr_max(tm.to(dev), ws, spec.to(dev), mx, am, H, W,
+                                   template_index_base=base, reset=reset)
+    torch.cuda.synchronize()
+    return mx, am
+
+
+@pytest.mark.parametrize("B,h,w,H,W,full", [(6, 16, 16, 64, 64, True), (5, 40, 30, 256, 512, False),
+                                            (9, 100, 100, 1024, 1024, True),
+                                            (4, 384, 384, 3840, 3840, True)])
+def test_corr_max_matches_oracle(B, h, w, H, W, full):
+    _, tm, spec = make_inputs(B, h, w, H, W, seed=B + h)
+    mx, am = run_corr_max(tm, spec, H, W, full)
+    ref = O.padded_corr2d_f64(tm.numpy(), spec.numpy(), H, W, True, full)
+    rmax, rarg, sure = maps(ref)
+    got_max, got_arg = mx.cpu().numpy(), am.cpu().numpy()
+    assert O.rel_l2(rmax, got_max) < 5e-6
+    assert O.max_abs_over_peak(rmax, got_max) < 1e-4
+    assert sure.mean() > 0.99
+    assert np.array_equal(got_arg[sure], rarg[sure])  # bit-exact where the margin is clear
+
+
+def test_corr_max_in_batches_equals_one_call():
+    _, tm, spec = make_inputs(7, 64, 64, 512, 512, seed=4)
+    mx1, am1 = run_corr_max(tm, spec, 512, 512, True)
+    mx2, am2 = run_corr_max(tm[:3], spec, 512, 512, True, base=0, reset=True)
+    run_corr_max(tm[3:], spec, 512, 512, True, base=3, reset=False, mx=mx2, am=am2)
+    assert torch.equal(mx1, mx2) and torch.equal(am1, am2)
+
+
+def test_tie_keeps_lowest_index():
+    _, tm, spec = make_inputs(4, 32, 32, 256, 256, seed=8)
+    tm[3] = tm[1]  # identical templates: every pixel ties between 1 and 3
+    mx, am = run_corr_max(tm, spec, 256, 256, True)
+    assert not torch.any(am == 3)
+
+
+def test_pack_unpack_round_trip_and_order():
+    lib = _lib.load()
+    dev = torch.device("cuda", 0)
+    vals = torch.tensor([-3.5, -0.0, 0.0, 1e-30, 2.0, 2.0, float("inf"), -float("inf")], device=dev)
+    idx = torch.tensor([5, 1, 2, 3, 9, 4, 0, 7], dtype=torch.int32, device=dev)
+    keys = torch.empty(8, dtype=torch.int64, device=dev)
+    s = torch.cuda.current_stream().cuda_stream
+    _lib.check(lib.zfft_pack_max_arg(vals.data_ptr(), idx.data_ptr(), keys.data_ptr(), 8, 0, s))
+    v2 = torch.empty_like(vals)
+    i2 = torch.empty_like(idx)
+    _lib.check(lib.zfft_unpack_max_arg(keys.data_ptr(), v2.data_ptr(), i2.data_ptr(), 8, 0, s))
+    torch.cuda.synchronize()
+    assert torch.equal(vals.view(torch.int32), v2.view(torch.int32))  # bit-exact, incl. -0.0
+    assert torch.equal(idx, i2)
+    k = keys.cpu().tolist()
+    # larger value wins; equal values: lower index wins
+    assert k[4] < k[5] and max(k) == k[6] and min(k) == k[7] and k[0] < k[1] < k[2] < k[3]
+
+
+def test_search_planted_templates_known_answer():
+    """A reduced version of the full search: 256 templates of 384^2, copies of
+    template 77 planted at 20 positions with amplitude 0.5; the search finds
+    template 77 at exactly those positions."""
+    from zipfft_b200.search import template_search
+
+    H = 4096
+    rng = np.random.default_rng(50)
+    img = rng.standard_normal((H, H)).astype(np.float32)
+    g = torch.Generator().manual_seed(5)
+    tm = torch.randn((256, 384, 384), generator=g)
+    tm = (tm - tm.mean(dim=(1, 2), keepdim=True)) / tm.std(dim=(1, 2), keepdim=True)
+    k = 77
+    pos = set()
+    while len(pos) < 20:
+        y, x = (int(v) for v in rng.integers(0, H - 384, size=2))
+        if all(abs(y - a) > 400 or abs(x - b) > 400 for a, b in pos):
+            pos.add((y, x))
+    for (y, x) in pos:
+        img[y:y + 384, x:x + 384] += 0.5 * tm[k].numpy()
+    spec = torch.from_numpy(O.image_spectrum_T(img)).cuda()
+    mx, am = template_search(tm.pin_memory(), spec, H, H, batch_size=64, full=True)
+    torch.cuda.synchronize()
+    mx, am = mx.cpu().numpy(), am.cpu().numpy()
+    for (y, x) in pos:
+        assert am[y, x] == k
+        assert mx[y, x] > 0.4 * 384 * 384
+    top = np.argsort(mx.ravel())[::-1][:20]
+    assert sorted((int(i // H), int(i % H)) for i in top) == sorted(pos)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_search_two_gpus_nccl(tmp_path):
+    import subprocess
+    import sys
+
+    script = tmp_path / "run.py"
+    script.write_text(
+        "import os, sys, datetime, numpy as np, torch, torch.distributed as dist\n"
+        f"sys.path.insert(0, {repr(str(__import__('pathlib').Path(__file__).resolve().parents[1]))})\n"
+        "from oracle import xcorr_oracle as O\n"
+        "from zipfft_b200.search import template_search\n"
+        "r = int(os.environ['RANK']); torch.cuda.set_device(r)\n"
+        "dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=120),"
+        " device_id=torch.device('cuda', r))\n"
+        "g = torch.Generator().manual_seed(3)\n"
+        "img = torch.randn((512, 512), generator=g); tm = torch.randn((10, 40, 40), generator=g)\n"
+        "spec = torch.from_numpy(O.image_spectrum_T(img.numpy())).cuda()\n"
+        "mx, am = template_search(tm, spec, 512, 512, batch_size=3)\n"
+        "ref = O.padded_corr2d_f64(tm.numpy(), spec.cpu().numpy(), 512, 512, True, True)\n"
+        "order = np.sort(ref, 0); sure = (order[-1] - order[-2]) > 1e-4 * np.abs(ref).max()\n"
+        "ok = np.array_equal(am.cpu().numpy()[sure], ref.argmax(0)[sure]) and "
+        "O.rel_l2(ref.max(0), mx.cpu().numpy()) < 5e-6\n"
+        "dist.destroy_process_group(); sys.exit(0 if ok else 1)\n")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", "--master-port=29517", str(script)]
+    res = subprocess.run(cmd, capture_output=True, text=True, timeout=300,
+                         env={**__import__("os").environ, "NCCL_NVLS_ENABLE": "0"})
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-2000:]

@@ -28,6 +28,11 @@ SIGNATURES = {
     "zfft_padded_real_conv_2d": (_c_int, _CONV_ARGS),
     "zfft_padded_real_corr_2d_noalloc": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _vp, _c_int,
                                                   _c_int, _c_int, _c_int, _c_int, _vp]),
+    "zfft_padded_real_corr_2d_max": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _c_size, _vp, _vp,
+                                              _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                              _c_int, _vp]),
+    "zfft_pack_max_arg": (_c_int, [_vp, _vp, _vp, _c_size, _c_int, _vp]),
+    "zfft_unpack_max_arg": (_c_int, [_vp, _vp, _vp, _c_size, _c_int, _vp]),
     "zfft_workspace_bytes": (_c_size, [_c_int, _c_int]),
     "zfft_is_fft_size_supported": (_c_int, [_c_int]),
     "zfft_get_supported_conv_configs": (_c_int, [ctypes.POINTER(ctypes.c_int), _c_int]),

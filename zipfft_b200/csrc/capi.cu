@@ -196,8 +196,8 @@ using ColFn = cudaError_t (*)(float2*, const float2*, int, const float2*, const 
 using R2cFn = cudaError_t (*)(const float*, float2*, const float2*, int, int, int, long long, int,
                               float, int, int, cudaStream_t);
 using QmapFn = cudaError_t (*)(const float2*, int, CUtensorMap*);
-using C2rFn = cudaError_t (*)(const CUtensorMap*, float*, const float2*, int, int, int, int*, int,
-                              cudaStream_t);
+using C2rFn = cudaError_t (*)(const CUtensorMap*, float*, int*, const float2*, int, int, int, int,
+                              int, int*, int, cudaStream_t);
 
 ColFn col_fn(int n) {
 #define ZF_X(N) \
@@ -262,9 +262,13 @@ const int kConfigs[][6] = {
     {384, 384, 3840, 3840, 128, 1}, {384, 384, 4096, 4096, 256, 1},
 };
 
+// One call of the correlation path.  arg == nullptr: output holds `batch`
+// maps of oy x ox.  Otherwise output / arg are the running max / argmax maps
+// (oy x ox) that every template folds into, template t with index
+// tindex_base + t; reset: the first template overwrites them.
 int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes,
         const void* conv_data, float* output, int oy, int ox, int H, int W, bool conj,
-        int device, void* stream) {
+        int device, void* stream, int* arg = nullptr, int tindex_base = 0, bool reset = false) {
     g_last_error.clear();
     if (batch < 0) return fail(ZFFT_ERROR_INVALID_VALUE, "batch must be >= 0. Got %d.", batch);
     if (sy < 1 || sx < 1)
@@ -299,6 +303,7 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
     if (batch == 0) return ZFFT_SUCCESS;
     if (!input || !ws || !conv_data || !output)
         return fail(ZFFT_ERROR_INVALID_VALUE, "null data pointer");
+    if (arg && !aligned(arg, 4)) return fail(ZFFT_ERROR_INVALID_VALUE, "misaligned argmax map");
     if (!aligned(input, 4) || !aligned(output, 4) || !aligned(ws, 16) || !aligned(conv_data, 16))
         return fail(ZFFT_ERROR_INVALID_VALUE,
                     "misaligned pointer: input/output need 4-byte alignment, fft_workspace and "
@@ -386,7 +391,12 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
             timer_close(1, m, s);
             if ((e = trace_sync(s, "k_col_fused", t)) != cudaSuccess) return cuda_fail(e, "k_col_fused");
             m = timer_mark(s);
-            e = c2r(&qmap, output + (size_t)t * oy * ox, twW, oy, ox, ox, status, device, s);
+            if (arg)
+                e = c2r(&qmap, output, arg, twW, oy, ox, ox, tindex_base + t, (reset && t == 0) ? 1 : 0,
+                        status, device, s);
+            else
+                e = c2r(&qmap, output + (size_t)t * oy * ox, nullptr, twW, oy, ox, ox, 0, 0, status,
+                        device, s);
             if (e != cudaSuccess) return cuda_fail(e, "row c2r launch");
             timer_close(2, m, s);
             if ((e = trace_sync(s, "k_row_c2r", t)) != cudaSuccess) return cuda_fail(e, "k_row_c2r");
@@ -444,6 +454,37 @@ __global__ void k_wait_selftest(int* status, long long limit) {
     }
     const bool ok = mbar_wait_bounded(&bar, 0, limit);
     if (__syncthreads_or(!ok) && threadIdx.x == 0) atomicExch(status, kStatusTimeout);
+}
+
+// Order-preserving 64-bit keys of (max, argmax) pairs for one integer MAX
+// reduction across GPUs: high 32 bits = the float's bits mapped to unsigned
+// order, low 32 bits = 0xFFFFFFFF - index (the lower index wins ties); the
+// sign bit is flipped so that signed comparison (NCCL int64 MAX) orders keys
+// like unsigned comparison.
+__device__ __forceinline__ long long pack_key(float v, int idx) {
+    uint32_t u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    const uint64_t k = (uint64_t(u) << 32) | uint64_t(0xFFFFFFFFu - uint32_t(idx));
+    return (long long)(k ^ 0x8000000000000000ull);
+}
+__device__ __forceinline__ void unpack_key(long long key, float* v, int* idx) {
+    const uint64_t k = uint64_t(key) ^ 0x8000000000000000ull;
+    uint32_t u = uint32_t(k >> 32);
+    u = (u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u;
+    *v = __uint_as_float(u);
+    *idx = int(0xFFFFFFFFu - uint32_t(k));
+}
+__global__ void k_pack_keys(const float* __restrict__ v, const int* __restrict__ idx,
+                            long long* __restrict__ keys, long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x)
+        keys[i] = pack_key(v[i], idx[i]);
+}
+__global__ void k_unpack_keys(const long long* __restrict__ keys, float* __restrict__ v,
+                              int* __restrict__ idx, long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x)
+        unpack_key(keys[i], v + i, idx + i);
 }
 
 cudaError_t launch_wait_selftest(int* status, long long limit_cycles, cudaStream_t s) {
@@ -514,6 +555,61 @@ int zfft_stage_timing_read(double* ms, int* launches, int n) {
 }
 
 int zfft_get_version(void) { return kVersion; }
+
+int zfft_padded_real_corr_2d_max(const float* input, int batch, int signal_y, int signal_x,
+                                 void* fft_workspace, size_t fft_workspace_bytes,
+                                 const void* conv_data, float* max_map, int32_t* arg_map,
+                                 int output_y, int output_x, int fft_size_y, int fft_size_x,
+                                 int template_index_base, int reset, int device, void* stream) {
+    if (!arg_map && batch > 0) return fail(ZFFT_ERROR_INVALID_VALUE, "null argmax map");
+    if (template_index_base < 0 || (long long)template_index_base + batch > 0x7FFFFFFFLL)
+        return fail(ZFFT_ERROR_INVALID_VALUE, "template indices must lie in [0, 2^31 - 1)");
+    return run(input, batch, signal_y, signal_x, fft_workspace, fft_workspace_bytes, conv_data,
+               max_map, output_y, output_x, fft_size_y, fft_size_x, true, device, stream,
+               reinterpret_cast<int*>(arg_map), template_index_base, reset != 0);
+}
+
+namespace {
+int launch_keys(bool pack, const float* v_in, float* v_out, const int32_t* i_in, int32_t* i_out,
+                const int64_t* k_in, int64_t* k_out, size_t n, int device, void* stream) {
+    g_last_error.clear();
+    if (n == 0) return ZFFT_SUCCESS;
+    int ndev = 0;
+    cudaError_t e = cudaGetDeviceCount(&ndev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+    if (device < 0 || device >= ndev || device >= kMaxDevices)
+        return fail(ZFFT_ERROR_INVALID_VALUE, "invalid device index %d (%d devices)", device, ndev);
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess) return cuda_fail(guard.err, "cudaSetDevice");
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    const long long blocks_needed = ((long long)n + 255) / 256;
+    const int grid = (int)(blocks_needed < 8LL * sms ? blocks_needed : 8LL * sms);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (pack) {
+        if (!v_in || !i_in || !k_out) return fail(ZFFT_ERROR_INVALID_VALUE, "null pointer");
+        zf::k_pack_keys<<<grid, 256, 0, s>>>(v_in, reinterpret_cast<const int*>(i_in),
+                                              reinterpret_cast<long long*>(k_out), (long long)n);
+    } else {
+        if (!k_in || !v_out || !i_out) return fail(ZFFT_ERROR_INVALID_VALUE, "null pointer");
+        zf::k_unpack_keys<<<grid, 256, 0, s>>>(reinterpret_cast<const long long*>(k_in), v_out,
+                                                reinterpret_cast<int*>(i_out), (long long)n);
+    }
+    e = cudaGetLastError();
+    return e == cudaSuccess ? ZFFT_SUCCESS : cuda_fail(e, "key kernel launch");
+}
+}  // namespace
+
+int zfft_pack_max_arg(const float* max_map, const int32_t* arg_map, int64_t* keys, size_t n,
+                      int device, void* stream) {
+    return launch_keys(true, max_map, nullptr, arg_map, nullptr, nullptr, keys, n, device, stream);
+}
+
+int zfft_unpack_max_arg(const int64_t* keys, float* max_map, int32_t* arg_map, size_t n, int device,
+                        void* stream) {
+    return launch_keys(false, nullptr, max_map, nullptr, arg_map, keys, nullptr, n, device, stream);
+}
 
 int zfft_padded_real_corr_2d_noalloc(const float* input, int batch, int signal_y, int signal_x,
                                      const void* conv_data, float* output, int output_y,

@@ -82,18 +82,20 @@ cudaError_t col_t(float2* Q, const float2* R, int r_pitch, const float2* spec, c
     return cudaGetLastError();
 }
 
-template <int W2>
-cudaError_t c2r_t(const CUtensorMap* qmap, float* out, const float2* tw, int out_rows,
-                  int out_cols, int out_pitch, int* status, int device, cudaStream_t s) {
+template <int W2, int MODE>
+cudaError_t c2r_t(const CUtensorMap* qmap, float* out, int* arg, const float2* tw, int out_rows,
+                  int out_cols, int out_pitch, int tindex, int reset, int* status, int device,
+                  cudaStream_t s) {
     using C = C2rCfg<W2>;
     static KernelState st;
-    auto kernel = k_row_c2r<W2>;
+    auto kernel = k_row_c2r<W2, MODE>;
     int cap = 0;
     cudaError_t e = configure(kernel, st, C::SMEM, C::THREADS, device, &cap);
     if (e != cudaSuccess) return e;
     const int groups = (out_rows + C::RPB - 1) / C::RPB;
     const int grid = min_int(groups, cap);
-    kernel<<<grid, C::THREADS, C::SMEM, s>>>(*qmap, out, tw, out_rows, out_cols, out_pitch, status);
+    kernel<<<grid, C::THREADS, C::SMEM, s>>>(*qmap, out, arg, tw, out_rows, out_cols, out_pitch,
+                                             tindex, reset, status);
     return cudaGetLastError();
 }
 
@@ -140,10 +142,15 @@ cudaError_t ZF_CAT(make_qmap_, ZF_SIZE)(const float2* Q, int H, CUtensorMap* map
                                 (unsigned long long)H * 8ull, C::RPB, C::BOXK);
 }
 
-cudaError_t ZF_CAT(launch_row_c2r_, ZF_SIZE)(const CUtensorMap* qmap, float* out, const float2* tw,
-                                             int out_rows, int out_cols, int out_pitch,
-                                             int* status, int device, cudaStream_t s) {
-    return c2r_t<ZF_SIZE / 2>(qmap, out, tw, out_rows, out_cols, out_pitch, status, device, s);
+cudaError_t ZF_CAT(launch_row_c2r_, ZF_SIZE)(const CUtensorMap* qmap, float* out, int* arg,
+                                             const float2* tw, int out_rows, int out_cols,
+                                             int out_pitch, int tindex, int reset, int* status,
+                                             int device, cudaStream_t s) {
+    if (arg != nullptr)
+        return c2r_t<ZF_SIZE / 2, kRunningMax>(qmap, out, arg, tw, out_rows, out_cols, out_pitch,
+                                               tindex, reset, status, device, s);
+    return c2r_t<ZF_SIZE / 2, kStoreMap>(qmap, out, nullptr, tw, out_rows, out_cols, out_pitch,
+                                         0, 0, status, device, s);
 }
 
 }  // namespace zf

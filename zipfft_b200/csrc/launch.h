@@ -16,7 +16,9 @@ namespace zf {
 // Column pass of an H-row image: forward FFT of the h rows of R, product with
 // the spectrum, inverse FFT, first store_rows rows of Q stored.
 // Row c2r: the Q tile map comes from make_qmap_<W> (same W); out_rows rows of
-// out_cols values at out_pitch.
+// out_cols values at out_pitch.  arg == nullptr: store the map into out;
+// otherwise fold it into the running max (out) / argmax (arg) maps with
+// template index tindex (reset: overwrite instead of compare).
 #define ZF_DECL(N)                                                                              \
     cudaError_t launch_row_r2c_##N(const float* tmpl, float2* R, const float2* tw, int h, int w, \
                                    int r_pitch, long long r_tstride, int ntemplates, float scale, \
@@ -25,9 +27,10 @@ namespace zf {
                                const float2* tw, int h, int W2, int store_rows, bool conj, int nz, \
                                bool discard_r, int* status, int device, cudaStream_t s);         \
     cudaError_t make_qmap_##N(const float2* Q, int H, CUtensorMap* map);                        \
-    cudaError_t launch_row_c2r_##N(const CUtensorMap* qmap, float* out, const float2* tw,        \
-                                   int out_rows, int out_cols, int out_pitch, int* status,       \
-                                   int device, cudaStream_t s);
+    cudaError_t launch_row_c2r_##N(const CUtensorMap* qmap, float* out, int* arg,               \
+                                   const float2* tw, int out_rows, int out_cols, int out_pitch,  \
+                                   int tindex, int reset, int* status, int device,               \
+                                   cudaStream_t s);
 ZF_FOR_EACH_FFT_SIZE(ZF_DECL)
 #undef ZF_DECL
 

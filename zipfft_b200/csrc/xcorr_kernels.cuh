@@ -395,11 +395,21 @@ struct C2rCfg {
     static constexpr int SMEM = FLOATS * 8 + 2 * 8;
 };
 
-template <int W2>
+// Epilogues of the inverse row pass.
+constexpr int kStoreMap = 0;  // write the correlation map
+constexpr int kRunningMax = 1;  // fold it into a running per-pixel max / argmax
+
+// MODE kStoreMap: out[y][x] = correlation.  MODE kRunningMax: out is the
+// running maximum map and arg the template-index map (same pitch); where the
+// correlation is strictly greater than the stored maximum (or everywhere when
+// `reset`), the maximum becomes the correlation and the index `tindex`.
+// Templates folded in increasing index order therefore keep the lowest index
+// on ties.
+template <int W2, int MODE>
 __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     k_row_c2r(const __grid_constant__ CUtensorMap qmap, float* __restrict__ out,
-              const float2* __restrict__ twW, int out_rows, int out_cols, int out_pitch,
-              int* __restrict__ status) {
+              int* __restrict__ arg, const float2* __restrict__ twW, int out_rows, int out_cols,
+              int out_pitch, int tindex, int reset, int* __restrict__ status) {
     using C = C2rCfg<W2>;
     using I = Stockham<W2, C::T, true, false>;
     static_assert(I::S >= 2, "row FFT needs at least two stages");
@@ -491,19 +501,77 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
         const int y = grp * C::RPB + g;
         if (y < out_rows) {
             float* orow = out + (size_t)y * out_pitch;
+            if constexpr (MODE == kStoreMap) {
 #pragma unroll
-            for (int q = 0; q < I::bpt(I::S - 1); ++q) {
-                const int bb = t + q * C::T;
-                if (I::even(I::S - 1) || bb < NBL) {
+                for (int q = 0; q < I::bpt(I::S - 1); ++q) {
+                    const int bb = t + q * C::T;
+                    if (I::even(I::S - 1) || bb < NBL) {
+#pragma unroll
+                        for (int r = 0; r < RL; ++r) {
+                            const int m = bb + r * NBL;
+                            const float2 z = v[q * RL + r];
+                            if (vec_ok) {
+                                st_hint(reinterpret_cast<float2*>(orow) + m, z, pol_stream);
+                            } else {
+                                if (2 * m < out_cols) st_hint(orow + 2 * m, z.x, pol_stream);
+                                if (2 * m + 1 < out_cols) st_hint(orow + 2 * m + 1, z.y, pol_stream);
+                            }
+                        }
+                    }
+                }
+            } else {
+                int* arow = arg + (size_t)y * out_pitch;
+                // All loads of the stored maxima first, then the updates.
+                float2 cur[I::bpt(I::S - 1) * RL];
+#pragma unroll
+                for (int q = 0; q < I::bpt(I::S - 1); ++q) {
+                    const int bb = t + q * C::T;
 #pragma unroll
                     for (int r = 0; r < RL; ++r) {
                         const int m = bb + r * NBL;
-                        const float2 z = v[q * RL + r];
-                        if (vec_ok) {
-                            st_hint(reinterpret_cast<float2*>(orow) + m, z, pol_stream);
-                        } else {
-                            if (2 * m < out_cols) st_hint(orow + 2 * m, z.x, pol_stream);
-                            if (2 * m + 1 < out_cols) st_hint(orow + 2 * m + 1, z.y, pol_stream);
+                        float2 c = c_make(-INFINITY, -INFINITY);
+                        if (!reset && (I::even(I::S - 1) || bb < NBL)) {
+                            if (vec_ok) {
+                                c = reinterpret_cast<const float2*>(orow)[m];
+                            } else {
+                                if (2 * m < out_cols) c.x = orow[2 * m];
+                                if (2 * m + 1 < out_cols) c.y = orow[2 * m + 1];
+                            }
+                        }
+                        cur[q * RL + r] = c;
+                    }
+                }
+#pragma unroll
+                for (int q = 0; q < I::bpt(I::S - 1); ++q) {
+                    const int bb = t + q * C::T;
+                    if (I::even(I::S - 1) || bb < NBL) {
+#pragma unroll
+                        for (int r = 0; r < RL; ++r) {
+                            const int m = bb + r * NBL;
+                            const float2 z = v[q * RL + r];
+                            const float2 c = cur[q * RL + r];
+                            const bool u0 = reset || z.x > c.x, u1 = reset || z.y > c.y;
+                            if (vec_ok) {
+                                if (u0 && u1) {
+                                    reinterpret_cast<float2*>(orow)[m] = z;
+                                    reinterpret_cast<int2*>(arow)[m] = make_int2(tindex, tindex);
+                                } else if (u0) {
+                                    orow[2 * m] = z.x;
+                                    arow[2 * m] = tindex;
+                                } else if (u1) {
+                                    orow[2 * m + 1] = z.y;
+                                    arow[2 * m + 1] = tindex;
+                                }
+                            } else {
+                                if (u0 && 2 * m < out_cols) {
+                                    orow[2 * m] = z.x;
+                                    arow[2 * m] = tindex;
+                                }
+                                if (u1 && 2 * m + 1 < out_cols) {
+                                    orow[2 * m + 1] = z.y;
+                                    arow[2 * m + 1] = tindex;
+                                }
+                            }
                         }
                     }
                 }

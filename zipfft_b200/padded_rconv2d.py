@@ -26,7 +26,7 @@ import torch
 
 from . import _lib
 
-__all__ = ["corr", "conv", "get_supported_conv_configs", "supported_fft_sizes",
+__all__ = ["corr", "conv", "corr_max", "get_supported_conv_configs", "supported_fft_sizes",
            "workspace_bytes"]
 
 
@@ -94,6 +94,9 @@ def _validate(input: torch.Tensor, fft_workspace: torch.Tensor, conv_data: torch
                                         "batch size")
     for name, t in (("Input", input), ("FFT workspace", fft_workspace),
                     ("Convolution data", conv_data), ("Output", output)):
+        # (an expanded view stands in for corr_max's per-template output)
+        if t is output and output.dim() == 3 and output.stride(0) == 0:
+            continue
         _check(t.is_contiguous(), f"{name} tensor must be contiguous")
     return batch, sy, sx, output.size(-2), output.size(-1)
 
@@ -128,6 +131,44 @@ def conv(input: torch.Tensor, fft_workspace: torch.Tensor, conv_data: torch.Tens
     """2D padded real convolution (binding.cu:288-292, :303); arguments as corr."""
     _run("zfft_padded_real_conv_2d", input, fft_workspace, conv_data, output, fft_size_y,
          fft_size_x)
+
+
+def corr_max(input: torch.Tensor, fft_workspace: torch.Tensor, conv_data: torch.Tensor,
+             max_map: torch.Tensor, arg_map: torch.Tensor, fft_size_y: int, fft_size_x: int,
+             template_index_base: int = 0, reset: bool = False) -> None:
+    """Cross-correlate every template like `corr`, folding the results into
+    running per-pixel maps instead of writing one map per template.
+
+    max_map (float32) keeps the largest correlation per pixel, arg_map (int32)
+    the index of the template that produced it; template t of `input` has
+    index template_index_base + t and ties keep the lower index.  Both maps
+    are (H-h+1, W-w+1) or (H, W).  reset=True: this call's first template
+    overwrites the maps (no initialisation needed).  No counterpart in the
+    reference; the 2D template-matching search its README motivates."""
+    _check(max_map.dtype == torch.float32, "Max map tensor must be of type torch.float32")
+    _check(arg_map.dtype == torch.int32, "Argmax map tensor must be of type torch.int32")
+    _check(max_map.dim() == 2 and arg_map.shape == max_map.shape,
+           "Max and argmax maps must be 2D tensors of the same shape")
+    _check(max_map.device == input.device and arg_map.device == input.device,
+           "Max and argmax maps must be on the same device as the input tensor")
+    _check(max_map.is_contiguous() and arg_map.is_contiguous(), "Maps must be contiguous")
+    lead = (input.size(0),) if input.dim() == 3 else ()
+    # Validate everything else exactly as corr does, with a shape stand-in for
+    # the per-template output.
+    batch, sy, sx, oy, ox = _validate(input, fft_workspace, conv_data,
+                                      max_map.expand(*lead, *max_map.shape), int(fft_size_y),
+                                      int(fft_size_x))
+    lib = _lib.load()
+    device = input.device.index if input.device.index is not None else torch.cuda.current_device()
+    stream = torch.cuda.current_stream(device).cuda_stream
+    ws_bytes = fft_workspace.numel() * fft_workspace.element_size()
+    status = lib.zfft_padded_real_corr_2d_max(input.data_ptr(), batch, sy, sx,
+                                              fft_workspace.data_ptr(), ws_bytes,
+                                              conv_data.data_ptr(), max_map.data_ptr(),
+                                              arg_map.data_ptr(), oy, ox, int(fft_size_y),
+                                              int(fft_size_x), int(template_index_base),
+                                              1 if reset else 0, device, stream)
+    _lib.check(status)
 
 
 def get_supported_conv_configs() -> List[Tuple[int, int, int, int, int, bool]]:

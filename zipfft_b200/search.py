@@ -1,0 +1,151 @@
+"""Multi-GPU 2D template matching: per-pixel maximum and argmax of the
+cross-correlation over a large template set.
+
+One process per GPU (torch.distributed, NCCL).  The image spectrum is
+replicated; the templates are split into contiguous shards, one per rank;
+every rank streams its shard through `padded_rconv2d.corr_max` in batches
+(templates copied from host memory on a side stream, double-buffered), and
+the per-rank maps are combined with a single all-reduce (MAX) of packed
+64-bit keys (order-preserving float bits high, inverted template index low,
+so ties keep the lowest index).  No data moves between GPUs before that one
+reduction.  The reference has no multi-GPU code; this is the search its
+README motivates (2DTM), sharded the way SURVEY's plan describes.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable, Optional, Tuple
+
+import torch
+
+from . import _lib
+
+
+def shard_range(n_templates: int, rank: int, world: int) -> Tuple[int, int]:
+    """Contiguous shard [lo, hi) of template indices for `rank`."""
+    base, extra = divmod(n_templates, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+@dataclass
+class SearchOps:
+    """The per-GPU operations of the search (the CUDA library by default).
+
+    corr_max(batch (n, h, w), workspace, conv_data, max_map, arg_map, H, W,
+             template_index_base, reset) folds n templates into the maps."""
+
+    corr_max: Callable
+    pack: Callable       # (max_map, arg_map) -> int64 keys
+    unpack: Callable     # (keys, max_map, arg_map) -> None (in place)
+    workspace: Callable  # (H, W, h, device) -> workspace tensor
+
+
+def search_workspace_elems(H: int, W: int, h: int, chunk: int = 16) -> int:
+    """complex64 elements of a workspace holding the intermediate plus the row
+    spectra of `chunk` templates (the library then transforms the rows of 16
+    templates per launch)."""
+    h_pad = (h + 1) // 2 * 2
+    return _lib.load().zfft_workspace_bytes(H, W) // 8 + chunk * (W // 2) * h_pad
+
+
+def _cuda_workspace(H: int, W: int, h: int, device) -> torch.Tensor:
+    return torch.empty(search_workspace_elems(H, W, h), dtype=torch.complex64, device=device)
+
+
+def _cuda_corr_max(batch, workspace, conv_data, max_map, arg_map, H, W, template_index_base,
+                   reset) -> None:
+    n, h, w = batch.shape
+    oy, ox = max_map.shape
+    dev = batch.device.index
+    st = _lib.load().zfft_padded_real_corr_2d_max(
+        batch.data_ptr(), n, h, w, workspace.data_ptr(), workspace.numel() * 8,
+        conv_data.data_ptr(), max_map.data_ptr(), arg_map.data_ptr(), oy, ox, H, W,
+        int(template_index_base), 1 if reset else 0, dev, torch.cuda.current_stream(dev).cuda_stream)
+    _lib.check(st)
+
+
+def _cuda_pack(max_map: torch.Tensor, arg_map: torch.Tensor) -> torch.Tensor:
+    keys = torch.empty(max_map.shape, dtype=torch.int64, device=max_map.device)
+    dev = max_map.device.index
+    _lib.check(_lib.load().zfft_pack_max_arg(max_map.data_ptr(), arg_map.data_ptr(),
+                                             keys.data_ptr(), max_map.numel(), dev,
+                                             torch.cuda.current_stream(dev).cuda_stream))
+    return keys
+
+
+def _cuda_unpack(keys: torch.Tensor, max_map: torch.Tensor, arg_map: torch.Tensor) -> None:
+    dev = keys.device.index
+    _lib.check(_lib.load().zfft_unpack_max_arg(keys.data_ptr(), max_map.data_ptr(),
+                                               arg_map.data_ptr(), keys.numel(), dev,
+                                               torch.cuda.current_stream(dev).cuda_stream))
+
+
+CUDA_OPS = SearchOps(_cuda_corr_max, _cuda_pack, _cuda_unpack, _cuda_workspace)
+
+
+def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y: int,
+                    fft_size_x: int, *, batch_size: int = 256, full: bool = True,
+                    group=None, device: Optional[torch.device] = None,
+                    ops: SearchOps = CUDA_OPS) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Maximum and argmax (global template index) of the correlation per pixel.
+
+    templates: (N, h, w) float32 -- the whole set (every rank passes the same
+    tensor, on the host (pinned memory is fastest) or on its device); each rank
+    correlates its contiguous shard.  conv_data: (W/2+1, H) complex64
+    spectrum on this rank's device.  Returns (max_map float32, arg_map int32),
+    (H, W) if `full` else the valid crop, identical on every rank."""
+    import torch.distributed as dist
+
+    distributed = dist.is_available() and dist.is_initialized()
+    world = dist.get_world_size(group) if distributed else 1
+    rank = dist.get_rank(group) if distributed else 0
+    dev = device or conv_data.device
+    N, h, w = templates.shape
+    H, W = int(fft_size_y), int(fft_size_x)
+    oy, ox = (H, W) if full else (H - h + 1, W - w + 1)
+    lo, hi = shard_range(N, rank, world)
+
+    max_map = torch.full((oy, ox), float("-inf"), dtype=torch.float32, device=dev)
+    arg_map = torch.full((oy, ox), -1, dtype=torch.int32, device=dev)
+    nb = min(batch_size, max(hi - lo, 1))
+    workspace = ops.workspace(H, W, h, dev)
+
+    on_host = templates.device.type == "cpu"
+    compute = torch.cuda.current_stream(dev) if dev.type == "cuda" else None
+    copy = torch.cuda.Stream(dev) if (on_host and dev.type == "cuda") else None
+    bufs = [torch.empty((nb, h, w), dtype=torch.float32, device=dev) for _ in range(2)] \
+        if on_host else None
+    events = [None, None]
+
+    def stage(i: int, b0: int, b1: int) -> torch.Tensor:
+        if not on_host:
+            return templates[b0:b1]
+        buf = bufs[i][: b1 - b0]
+        if copy is not None:
+            copy.wait_stream(compute) if events[i] is None else copy.wait_event(events[i])
+            with torch.cuda.stream(copy):
+                buf.copy_(templates[b0:b1], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(copy)
+            compute.wait_event(ev)
+        else:
+            buf.copy_(templates[b0:b1])
+        return buf
+
+    first = True
+    for j, b0 in enumerate(range(lo, hi, nb)):
+        b1 = min(b0 + nb, hi)
+        batch = stage(j % 2, b0, b1)
+        ops.corr_max(batch, workspace, conv_data, max_map, arg_map, H, W, b0, first)
+        first = False
+        if copy is not None:  # the buffer may be refilled once this batch's kernels ran
+            ev = torch.cuda.Event()
+            ev.record(compute)
+            events[j % 2] = ev
+
+    if world > 1:
+        keys = ops.pack(max_map, arg_map)
+        dist.all_reduce(keys, op=dist.ReduceOp.MAX, group=group)
+        ops.unpack(keys, max_map, arg_map)
+    return max_map, arg_map
