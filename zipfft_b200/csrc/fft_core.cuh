@@ -491,69 +491,6 @@ struct Stockham {
         }
     }
 
-    // Ping-pong form of run_from: the exchanges alternate between two buffers
-    // (first b0, then b1, ...), so each needs one barrier instead of two: a
-    // buffer is written again only after the barrier of the following
-    // exchange, which every reader of it has passed.  hook(e) runs right after
-    // the barrier of this transform's e-th exchange (e = 0, 1, ...).
-    static constexpr int exchanges_from(int s) { return S - s; }
-    template <int s, int E = 0, class TWS, class HK>
-    ZF_DEV static void run_pp(float2 (&v)[MAXE], float2* b0, float2* b1, const TWS& tw, int t,
-                              HK&& hook) {
-        if constexpr (s < S) {
-            store<s - 1>(v, b0, t);
-            __syncthreads();
-            hook(E);
-            load<s>(v, b0, t);
-            compute<s>(v, tw);
-            run_pp<s + 1, E + 1>(v, b1, b0, tw, t, hook);
-        }
-    }
-
-    // Pruned-start forward transform (NZ in {1, 2}) in ping-pong form: the
-    // stage-0 outputs are formed directly in stage 1's registers (see
-    // run_loader), then stages 2.. exchange through b0, b1, b0, ...
-    // (NZ = 0: the full stage 0 from the loader, then stages 1.. in ping-pong form.)
-    // Number of exchanges run_loader_pp makes.
-    static constexpr int loader_exchanges(int nz) { return (nz == 1 || nz == 2) ? S - 2 : S - 1; }
-    template <int NZ, class LD, class TWS, class HK>
-    ZF_DEV static void run_loader_pp(float2 (&v)[MAXE], const LD& ld, float2* b0, float2* b1,
-                                     const TWS& tw, int t, HK&& hook) {
-        static_assert(S >= 2, "ping-pong loader needs two stages");
-        if constexpr (!(NZ == 1 || NZ == 2)) {
-            constexpr int R0 = radix(0), NB0 = nbf(0);
-#pragma unroll
-            for (int q = 0; q < bpt(0); ++q) {
-                const int b = t + q * T;
-                if (even(0) || b < NB0) {
-#pragma unroll
-                    for (int r = 0; r < R0; ++r) v[q * R0 + r] = ld(b + r * NB0);
-                }
-            }
-            compute<0>(v, tw);
-            run_pp<1>(v, b0, b1, tw, t, hook);
-            return;
-        }
-        constexpr int R0 = radix(0), NB0 = nbf(0), R1 = radix(1), NB1 = nbf(1);
-#pragma unroll
-        for (int q = 0; q < bpt(1); ++q) {
-            const int b = t + q * T;
-            if (even(1) || b < NB1) {
-                float2 w = tw.r0[q];
-                if (INV) w = c_conj(w);
-#pragma unroll
-                for (int r = 0; r < R1; ++r) {
-                    const int m = (b + r * NB1) / R0;
-                    float2 acc = ld(m);
-                    if constexpr (NZ == 2) acc = c_add(acc, c_mul(ld(m + NB0), w));
-                    v[q * R1 + r] = acc;
-                }
-            }
-        }
-        compute<1>(v, tw);
-        run_pp<2>(v, b0, b1, tw, t, hook);
-    }
-
     // Full transform whose stage-0 input is in registers (layout of stage 0).
     template <class TWS>
     ZF_DEV static void run_regs(float2 (&v)[MAXE], float2* buf, const TWS& tw, int t) {

@@ -183,9 +183,8 @@ struct ColCfg {
     static constexpr int SB = round_up(H, 16);                     // spectrum column
     static constexpr int NB0 = H / make_plan(H).R[0];
     static constexpr int RB = round_up(NZ > 0 ? NZ * NB0 : H, 16);  // template column
-    // two exchange buffers (ping-pong), one spectrum and one template column
-    static constexpr int FLOATS = FPB * (2 * XB + SB + RB);
-    static constexpr int SMEM = FLOATS * 8 + 8;  // + one mbarrier
+    static constexpr int FLOATS = FPB * (XB + 2 * SB + 2 * RB);
+    static constexpr int SMEM = FLOATS * 8 + 2 * 8;  // + two mbarriers
 };
 
 template <int H, bool CONJ, int NZ>
@@ -204,17 +203,18 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
     const int tid = threadIdx.x;
     const int g = tid / C::T, t = tid % C::T;
     float2* smem = dyn_smem();
-    float2* xb[2] = {smem + g * C::XB, smem + (C::FPB + g) * C::XB};
-    float2* sbase = smem + 2 * C::FPB * C::XB;        // [FPB][SB]
-    float2* rbase = sbase + C::FPB * C::SB;           // [FPB][RB]
-    uint64_t* mbar = reinterpret_cast<uint64_t*>(rbase + C::FPB * C::RB);
+    float2* xbuf = smem + g * C::XB;
+    float2* sbase = smem + C::FPB * C::XB;            // [2][FPB][SB]
+    float2* rbase = sbase + 2 * C::FPB * C::SB;       // [2][FPB][RB]
+    uint64_t* mbar = reinterpret_cast<uint64_t*>(rbase + 2 * C::FPB * C::RB);
 
     // Template-column buffers are zero beyond h: the pruned start reads them
     // unconditionally.  TMA later overwrites only the first round_up(h, 2).
-    for (int i = tid; i < C::FPB * C::RB; i += C::THREADS) rbase[i] = c_make(0.f, 0.f);
+    for (int i = tid; i < 2 * C::FPB * C::RB; i += C::THREADS) rbase[i] = c_make(0.f, 0.f);
     __syncthreads();
     if (tid == 0) {  // after the zero fill: orders it before the first TMA write
         mbar_init(&mbar[0], 1);
+        mbar_init(&mbar[1], 1);
         mbar_init_fence();
     }
     __syncthreads();
@@ -233,44 +233,45 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
     const uint64_t pol_stream = l2_evict_first();
     const uint64_t pol_keep = l2_evict_last();
 
-    // Thread 0 fetches the spectrum and template columns of group vc0.  The
-    // buffers are single: a group's copy is issued once the previous group
-    // has read them (after the inverse transform's first exchange barrier).
-    auto issue = [&](int vc0) {
+    // Thread 0 fetches the spectrum and template columns of group vc0 into buffer b.
+    auto issue = [&](int b, int vc0) {
         uint32_t bytes = 0;
         for (int j = 0; j < C::FPB; ++j)
             if (vc0 + j <= W2) bytes += H * 8u + r_bytes;
-        mbar_arrive_expect_tx(&mbar[0], bytes);
+        mbar_arrive_expect_tx(&mbar[b], bytes);
         for (int j = 0; j < C::FPB; ++j) {
             const int vc = vc0 + j;
             if (vc > W2) break;
-            tma_load_1d(sbase + j * C::SB, spec + (size_t)vc * H, H * 8u, &mbar[0], pol_stream);
+            tma_load_1d(sbase + (b * C::FPB + j) * C::SB, spec + (size_t)vc * H, H * 8u, &mbar[b],
+                        pol_stream);
             const int rc = vc == W2 ? 0 : vc;
-            tma_load_1d(rbase + j * C::RB, R + (size_t)rc * r_pitch, r_bytes, &mbar[0], pol_stream);
+            tma_load_1d(rbase + (b * C::FPB + j) * C::RB, R + (size_t)rc * r_pitch, r_bytes,
+                        &mbar[b], pol_stream);
         }
     };
 
-    // Exchange-buffer parity: the forward and inverse transforms continue one
-    // alternating sequence across columns.
-    constexpr int EXF = F::loader_exchanges(NZ);
-    constexpr int EXI = I::exchanges_from(1);
-    int p = 0;
-
     int vc0 = blockIdx.x * C::FPB;
-    if (tid == 0 && vc0 <= W2) issue(vc0);
+    if (tid == 0 && vc0 <= W2) issue(0, vc0);
     for (int it = 0; vc0 <= W2; ++it, vc0 += stride) {
+        const int b = it & 1;
+        const uint32_t parity = (it >> 1) & 1;
+        // The other buffer was last read before this iteration's barriers.
         const bool more = vc0 + stride <= W2;
-        const bool ok = mbar_wait_bounded(&mbar[0], (uint32_t)(it & 1));
+        if (tid == 0 && more) issue(b ^ 1, vc0 + stride);
+        const bool ok = mbar_wait_bounded(&mbar[b], parity);
         if (__syncthreads_or(!ok)) {
-            if (tid == 0) atomicExch(status, kStatusTimeout);
-            return;  // nothing else is in flight: the copies are single-buffered
+            if (tid == 0) {
+                atomicExch(status, kStatusTimeout);
+                if (more) mbar_wait_bounded(&mbar[b ^ 1], ((it + 1) >> 1) & 1);
+            }
+            return;
         }
 
         const int vc = vc0 + g;
         const bool active = vc <= W2;
         const int mode = vc == 0 ? 1 : (vc == W2 ? 2 : 0);
-        const float2* rcol = rbase + g * C::RB;
-        const float2* scol = sbase + g * C::SB;
+        const float2* rcol = rbase + (b * C::FPB + g) * C::RB;
+        const float2* scol = sbase + (b * C::FPB + g) * C::SB;
         // A template column outside Q (the chunked layout) has no other reader
         // once copied: drop its whole 128-byte lines from L2 without write-back.
         // Packed column 0 is read by two column kinds and is kept.
@@ -282,7 +283,6 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
                 l2_discard_line(reinterpret_cast<const void*>(a));
         }
 
-        auto no_hook = [](int) {};
         // The template buffer is zero past h (zero fill beyond the copied
         // length; the row kernel writes the padding row of an odd h), so the
         // loader reads it unconditionally.
@@ -292,11 +292,11 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
             // keeps the block barriers inside the transform convergent.
             if (mode == 0) {
                 auto ld = [&](int i) { return rcol[i]; };
-                F::template run_loader_pp<NZ>(v, ld, xb[p], xb[p ^ 1], twf, t, no_hook);
+                F::template run_loader<NZ>(v, ld, xbuf, twf, t);
             } else {
                 const float* rf = reinterpret_cast<const float*>(rcol) + (mode == 2 ? 1 : 0);
                 auto ld = [&](int i) { return c_make(rf[2 * i], 0.f); };
-                F::template run_loader_pp<NZ>(v, ld, xb[p], xb[p ^ 1], twf, t, no_hook);
+                F::template run_loader<NZ>(v, ld, xbuf, twf, t);
             }
         } else {
             // Groups of one block may hold different column kinds: one loader
@@ -307,9 +307,8 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
                 const float2 x = rcol[i];
                 return c_make(take_im ? x.y : x.x, keep_im ? x.y : 0.f);
             };
-            F::template run_loader_pp<NZ>(v, ld, xb[p], xb[p ^ 1], twf, t, no_hook);
+            F::template run_loader<NZ>(v, ld, xbuf, twf, t);
         }
-        const int pi = p ^ (EXF & 1);
 
         // Pointwise product with the image spectrum column (cuh:86-111).
 #pragma unroll
@@ -326,18 +325,11 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
             }
         }
 
-        // After the inverse's first exchange barrier every thread has read
-        // this group's spectrum and template columns: fetch the next group's.
-        auto prefetch = [&](int e) {
-            if (e == 0 && tid == 0 && more) issue(vc0 + stride);
-        };
-        I::template compute<0>(v, twf);  // stage 0 has no twiddles
         if constexpr (kShare) {
-            I::template run_pp<1>(v, xb[pi], xb[pi ^ 1], twf, t, prefetch);
+            I::run_regs(v, xbuf, twf, t);
         } else {
-            I::template run_pp<1>(v, xb[pi], xb[pi ^ 1], twi_own, t, prefetch);
+            I::run_regs(v, xbuf, twi_own, t);
         }
-        p ^= (EXF + EXI) & 1;
 
         if (active) {
             const bool full = store_rows >= H;
@@ -399,9 +391,8 @@ struct C2rCfg {
     static constexpr int XB = RPB == 2 ? round_up(spad_size(W2) - 8, 16) + 8 : xbuf_len(W2);
     static constexpr int BOXK = tma_box(W2);
     static constexpr int QB = round_up(W2 * RPB, 16);  // one Q tile
-    // one Q tile (single-buffered) and two exchange buffer sets (ping-pong)
-    static constexpr int FLOATS = QB + 2 * RPB * XB;
-    static constexpr int SMEM = FLOATS * 8 + 8;
+    static constexpr int FLOATS = 2 * QB + RPB * XB;
+    static constexpr int SMEM = FLOATS * 8 + 2 * 8;
 };
 
 // Epilogues of the inverse row pass.
@@ -429,12 +420,13 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     const int tid = threadIdx.x;
     const int g = tid % C::RPB, t = tid / C::RPB;
     float2* smem = dyn_smem();
-    float2* qtile = smem;                                    // [W2][RPB]
-    float2* xb[2] = {smem + C::QB + g * C::XB, smem + C::QB + (C::RPB + g) * C::XB};
+    float2* qbase = smem;                       // [2][W2][RPB]
+    float2* xbuf = smem + 2 * C::QB + g * C::XB;
     uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + C::FLOATS);
 
     if (tid == 0) {
         mbar_init(&mbar[0], 1);
+        mbar_init(&mbar[1], 1);
         mbar_init_fence();
     }
     __syncthreads();
@@ -458,30 +450,31 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     // overwrites them there without a DRAM round trip); output rows stream out.
     const uint64_t pol_keep = l2_evict_last();
     const uint64_t pol_stream = l2_evict_first();
-    // The tile buffer is single: a group's tile is fetched once the previous
-    // group's first stage has read the previous tile (after its first exchange
-    // barrier).
-    auto issue = [&](int grp) {
-        mbar_arrive_expect_tx(&mbar[0], (uint32_t)(W2 * C::RPB * 8));
+    auto issue = [&](int b, int grp) {
+        mbar_arrive_expect_tx(&mbar[b], (uint32_t)(W2 * C::RPB * 8));
         for (int k0 = 0; k0 < W2; k0 += C::BOXK)
-            tma_load_2d(qtile + k0 * C::RPB, &qmap, grp * C::RPB, k0, &mbar[0], pol_keep);
+            tma_load_2d(qbase + b * C::QB + k0 * C::RPB, &qmap, grp * C::RPB, k0, &mbar[b],
+                        pol_keep);
     };
-    // Exchange-buffer parity across groups.
-    constexpr int EXI = I::exchanges_from(1);
-    int p = 0;
 
     int grp = blockIdx.x;
-    if (tid == 0 && grp < ngroups) issue(grp);
+    if (tid == 0 && grp < ngroups) issue(0, grp);
     for (int it = 0; grp < ngroups; ++it, grp += gridDim.x) {
+        const int b = it & 1;
+        const uint32_t parity = (it >> 1) & 1;
         const bool more = grp + (int)gridDim.x < ngroups;
-        const bool ok = mbar_wait_bounded(&mbar[0], (uint32_t)(it & 1));
+        if (tid == 0 && more) issue(b ^ 1, grp + gridDim.x);
+        const bool ok = mbar_wait_bounded(&mbar[b], parity);
         if (__syncthreads_or(!ok)) {
-            if (tid == 0) atomicExch(status, kStatusTimeout);
-            return;  // nothing else is in flight: the tile is single-buffered
+            if (tid == 0) {
+                atomicExch(status, kStatusTimeout);
+                if (more) mbar_wait_bounded(&mbar[b ^ 1], ((it + 1) >> 1) & 1);
+            }
+            return;
         }
 
         // Stage 0 reads with the split pre-pass fused in: element k of row g.
-        const float2* qt = qtile + g;
+        const float2* qt = qbase + b * C::QB + g;
         float2 v[I::MAXE];
 #pragma unroll
         for (int q = 0; q < I::bpt(0); ++q) {
@@ -503,12 +496,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                 });
             }
         }
-        auto prefetch = [&](int e) {
-            if (e == 0 && tid == 0 && more) issue(grp + gridDim.x);
-        };
-        I::template compute<0>(v, tw);
-        I::template run_pp<1>(v, xb[p], xb[p ^ 1], tw, t, prefetch);
-        p ^= EXI & 1;
+        I::run_regs(v, xbuf, tw, t);
 
         const int y = grp * C::RPB + g;
         if (y < out_rows) {
