@@ -382,7 +382,9 @@ constexpr int tma_box(int n) {
 template <int W2>
 struct C2rCfg {
     static constexpr int T = fft_threads(W2);
-    static constexpr int RPB = cmax(2, 128 / T);  // rows per block (even: TMA x alignment)
+    // rows per block (even: TMA x alignment).  Each TMA tile row is a run of
+    // RPB intermediate values: 4 rows make it one 32-byte sector.
+    static constexpr int RPB = cmax(4, (256 / T) & ~1);
     static constexpr int THREADS = RPB * T;
     static constexpr int MINB = cmax(1, 512 / THREADS);
     // Rows are interleaved across lanes (row = tid % RPB): the tile reads of
