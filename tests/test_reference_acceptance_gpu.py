@@ -36,7 +36,12 @@ def repeats(fy, fx, batch):
 
 def run_conv_or_corr_2d_test(signal_length_y, signal_length_x, fft_size_y, fft_size_x,
                              batch_size, cross_correlate, dtype=torch.float32, rtol=RTOL,
-                             atol=ATOL, device="cuda:0"):
+                             atol=ATOL, device="cuda:0", seed=0):
+    # Inputs are seeded here; the reference draws them unseeded.  Its small-size
+    # check (allclose with rtol applied to |output|) fails whenever an output
+    # lands within ~1e-6 of zero while two fp32 FFTs differ there by their
+    # normal ~1e-7 relative rounding, so an unseeded run flakes at random.
+    torch.manual_seed(seed)
     filter_shape = (signal_length_y, signal_length_x)
     image_shape = (fft_size_y, fft_size_x)
     output_shape = (fft_size_y - signal_length_y + 1, fft_size_x - signal_length_x + 1)
@@ -87,31 +92,32 @@ def run_conv_or_corr_2d_test(signal_length_y, signal_length_x, fft_size_y, fft_s
 @pytest.mark.parametrize("signal_length_y,signal_length_x,fft_size_y,fft_size_x,batch_size",
                          CONV_CONFIGS)
 def test_convolution_2d(signal_length_y, signal_length_x, fft_size_y, fft_size_x, batch_size):
-    for _ in range(repeats(fft_size_y, fft_size_x, batch_size)):
+    for rep in range(repeats(fft_size_y, fft_size_x, batch_size)):
         run_conv_or_corr_2d_test(signal_length_y, signal_length_x, fft_size_y, fft_size_x,
-                                 batch_size, cross_correlate=False)
+                                 batch_size, cross_correlate=False, seed=rep)
 
 
 @pytest.mark.parametrize("signal_length_y,signal_length_x,fft_size_y,fft_size_x,batch_size",
                          CROSS_CORR_CONFIGS)
 def test_cross_correlation_2d(signal_length_y, signal_length_x, fft_size_y, fft_size_x,
                               batch_size):
-    for _ in range(repeats(fft_size_y, fft_size_x, batch_size)):
+    for rep in range(repeats(fft_size_y, fft_size_x, batch_size)):
         run_conv_or_corr_2d_test(signal_length_y, signal_length_x, fft_size_y, fft_size_x,
-                                 batch_size, cross_correlate=True)
+                                 batch_size, cross_correlate=True, seed=rep)
 
 
 def test_non_standard_stream():
     stream = torch.cuda.Stream()
     sy, sx, fy, fx, b = CONV_CONFIGS[0]
-    for _ in range(10):
+    for rep in range(10):
         with torch.cuda.stream(stream):
-            run_conv_or_corr_2d_test(sy, sx, fy, fx, b, cross_correlate=False)
+            run_conv_or_corr_2d_test(sy, sx, fy, fx, b, cross_correlate=False, seed=rep)
     stream.synchronize()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="Less than 2 CUDA devices available")
 def test_non_standard_device():
     sy, sx, fy, fx, b = CROSS_CORR_CONFIGS[0]
-    for _ in range(10):
-        run_conv_or_corr_2d_test(sy, sx, fy, fx, b, cross_correlate=True, device="cuda:1")
+    for rep in range(10):
+        run_conv_or_corr_2d_test(sy, sx, fy, fx, b, cross_correlate=True, device="cuda:1",
+                                 seed=rep)
