@@ -146,6 +146,16 @@ void zf::emu_discard_line(const void* p) {
         std::abort();
     }
 }
+// Bulk store rules: 16-byte aligned addresses and sizes, source inside the
+// block's shared memory.
+void zf::emu_check_store(const void* dst, const void* src, uint32_t bytes) {
+    const auto d = reinterpret_cast<uintptr_t>(dst), s = reinterpret_cast<uintptr_t>(src);
+    const auto lo = reinterpret_cast<uintptr_t>(emu_smem);
+    if (d % 16 || s % 16 || bytes % 16 || s < lo || s + bytes > lo + emu_smem_bytes) {
+        std::fprintf(stderr, "bad bulk store dst=%p src=%p bytes=%u\n", dst, src, bytes);
+        std::abort();
+    }
+}
 // TMA rules: 16-byte aligned addresses and sizes, destination inside the
 // block's shared memory.
 void zf::emu_check_copy(const void* dst, const void* src, uint32_t bytes) {
@@ -234,7 +244,7 @@ void run_c2r(const float2* Q, int H, float* out, int* arg, const float2* tw, int
                    map, out, (int*)nullptr, tw, orows, ocols, ocols, 0, 0, &g_status);
 }
 
-#define EMU_SIZES(X) X(64) X(128) X(256) X(512) X(120) X(240)
+#define EMU_SIZES(X) X(64) X(128) X(256) X(512) X(2048) X(120) X(240)
 
 static void col(int H, bool conj, int nz, float2* Q, const float2* R, int rp, const float2* spec,
                 const float2* tw, int h, int W2, int rows, int cap) {

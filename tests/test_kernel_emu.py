@@ -89,6 +89,8 @@ CASES = [
     (5, 16, 16, 64, 64, True, True, None, None, 2),  # chunked rows, partial last chunk
     (3, 9, 13, 128, 256, False, False, None, None, 3),  # chunked, odd template
     (4, 30, 30, 256, 256, True, True, 2, 2, 4),
+    (2, 100, 20, 2048, 64, True, True, 1, None, 2),   # one column per block: bulk column stores
+    (1, 129, 9, 2048, 64, False, False, 2, None, 0),  # valid crop, odd store length
 ]
 
 

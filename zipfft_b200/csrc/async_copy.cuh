@@ -104,6 +104,24 @@ ZF_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_
         : "memory");
 }
 
+// 1D bulk store shared -> global (both addresses 16-byte aligned, bytes a
+// multiple of 16), tracked as a bulk async-group of the issuing thread.
+ZF_DEV void tma_store_1d(void* dst, const void* src, uint32_t bytes, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.global.shared::cta.bulk_group.L2::cache_hint [%0], [%1], %2, %3;" ::"l"(dst),
+        "r"(smem_u32(src)), "r"(bytes), "l"(pol)
+        : "memory");
+}
+ZF_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until the issuing thread's bulk stores have finished reading shared
+// memory (the source may then be overwritten).
+ZF_DEV void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Wait until the issuing thread's bulk stores have completed.
+ZF_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Order this thread's generic shared-memory writes before later async-proxy
+// reads of them (a bulk store issued after a barrier).
+ZF_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // 8-byte store with an L2 eviction policy.
 ZF_DEV void st_hint(float2* p, float2 v, uint64_t pol) {
     asm volatile("st.global.L2::cache_hint.v2.f32 [%0], {%1, %2}, %3;" ::"l"(p), "f"(v.x),
@@ -152,6 +170,15 @@ inline void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* ba
     std::memcpy(dst, src, bytes);
     emu_mbar_complete_tx(bar, bytes);
 }
+void emu_check_store(const void* dst, const void* src, uint32_t bytes);
+inline void tma_store_1d(void* dst, const void* src, uint32_t bytes, uint64_t) {
+    emu_check_store(dst, src, bytes);
+    std::memcpy(dst, src, bytes);
+}
+inline void bulk_commit() {}
+inline void bulk_wait_read() {}
+inline void bulk_wait_all() {}
+inline void fence_proxy_async() {}
 inline void st_hint(float2* p, float2 v, uint64_t) { *p = v; }
 inline void st_hint(float* p, float v, uint64_t) { *p = v; }
 void emu_discard_line(const void* p);

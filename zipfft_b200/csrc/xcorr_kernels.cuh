@@ -259,10 +259,14 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
         const bool more = vc0 + stride <= W2;
         if (tid == 0 && more) issue(b ^ 1, vc0 + stride);
         const bool ok = mbar_wait_bounded(&mbar[b], parity);
+        // The previous column's bulk store must have read the exchange buffer
+        // before this column writes it (the barrier below publishes that).
+        if (tid == 0) bulk_wait_read();
         if (__syncthreads_or(!ok)) {
             if (tid == 0) {
                 atomicExch(status, kStatusTimeout);
                 if (more) mbar_wait_bounded(&mbar[b ^ 1], ((it + 1) >> 1) & 1);
+                bulk_wait_all();
             }
             return;
         }
@@ -331,6 +335,29 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
             I::run_regs(v, xbuf, twi_own, t);
         }
 
+        if constexpr (C::FPB == 1) {
+            if (mode == 0) {  // block-uniform (one column per block)
+                // Stage the column in the exchange buffer (its last reader
+                // finished before the transform's final barrier) and store it
+                // with one bulk copy.
+#pragma unroll
+                for (int q = 0; q < I::bpt(I::S - 1); ++q) {
+                    const int bb = t + q * C::T;
+                    if (I::even(I::S - 1) || bb < NBO) {
+#pragma unroll
+                        for (int r = 0; r < RO; ++r) xbuf[bb + r * NBO] = v[q * RO + r];
+                    }
+                }
+                fence_proxy_async();
+                __syncthreads();
+                if (tid == 0) {
+                    const int rows = store_rows >= H ? H : ((store_rows + 1) & ~1);
+                    tma_store_1d(Q + (size_t)vc * H, xbuf, (uint32_t)rows * 8u, pol_keep);
+                    bulk_commit();
+                }
+                continue;
+            }
+        }
         if (active) {
             const bool full = store_rows >= H;
             if (mode == 0) {
@@ -362,6 +389,7 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
             }
         }
     }
+    if (tid == 0) bulk_wait_all();
 }
 
 // ===========================================================================
@@ -382,9 +410,9 @@ constexpr int tma_box(int n) {
 template <int W2>
 struct C2rCfg {
     static constexpr int T = fft_threads(W2);
-    // rows per block (even: TMA x alignment).  Each TMA tile row is a run of
-    // RPB intermediate values: 4 rows make it one 32-byte sector.
-    static constexpr int RPB = cmax(4, (256 / T) & ~1);
+    // rows per block (even: TMA x alignment); two blocks of 256 threads per SM
+    // at W2 = 2048.
+    static constexpr int RPB = cmax(2, (128 / T) & ~1);
     static constexpr int THREADS = RPB * T;
     static constexpr int MINB = cmax(1, 512 / THREADS);
     // Rows are interleaved across lanes (row = tid % RPB): the tile reads of
@@ -392,7 +420,10 @@ struct C2rCfg {
     // buffers 16 banks apart keep the stage exchanges conflict free.
     static constexpr int XB = RPB == 2 ? round_up(spad_size(W2) - 8, 16) + 8 : xbuf_len(W2);
     static constexpr int BOXK = tma_box(W2);
-    static constexpr int QB = round_up(W2 * RPB, 16);  // one Q tile
+    // One Q tile; after the first stage has read it, the same buffer stages
+    // the block's output rows (row stride W2 + 8: rows 16 banks apart).
+    static constexpr int OROW = W2 + 8;
+    static constexpr int QB = round_up(cmax(W2 * RPB, OROW * RPB), 16);
     static constexpr int FLOATS = 2 * QB + RPB * XB;
     static constexpr int SMEM = FLOATS * 8 + 2 * 8;
 };
@@ -459,18 +490,29 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                         pol_keep);
     };
 
+    // Full-width maps leave through bulk stores of whole rows staged in
+    // shared memory (row starts are 16-byte aligned); cropped maps use
+    // per-thread stores.
+    const bool bulk_out = MODE == kStoreMap && vec_ok && (out_pitch % 4) == 0 &&
+                          (reinterpret_cast<size_t>(out) % 16) == 0;
     int grp = blockIdx.x;
     if (tid == 0 && grp < ngroups) issue(0, grp);
     for (int it = 0; grp < ngroups; ++it, grp += gridDim.x) {
         const int b = it & 1;
         const uint32_t parity = (it >> 1) & 1;
         const bool more = grp + (int)gridDim.x < ngroups;
-        if (tid == 0 && more) issue(b ^ 1, grp + gridDim.x);
+        if (tid == 0 && more) {
+            // buffer b^1 staged the previous group's rows: their bulk stores
+            // must have read it before the next tile lands there
+            bulk_wait_read();
+            issue(b ^ 1, grp + gridDim.x);
+        }
         const bool ok = mbar_wait_bounded(&mbar[b], parity);
         if (__syncthreads_or(!ok)) {
             if (tid == 0) {
                 atomicExch(status, kStatusTimeout);
                 if (more) mbar_wait_bounded(&mbar[b ^ 1], ((it + 1) >> 1) & 1);
+                bulk_wait_all();
             }
             return;
         }
@@ -503,7 +545,17 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
         const int y = grp * C::RPB + g;
         if (y < out_rows) {
             float* orow = out + (size_t)y * out_pitch;
-            if constexpr (MODE == kStoreMap) {
+            if (MODE == kStoreMap && bulk_out) {
+                float2* srow = qbase + b * C::QB + g * C::OROW;
+#pragma unroll
+                for (int q = 0; q < I::bpt(I::S - 1); ++q) {
+                    const int bb = t + q * C::T;
+                    if (I::even(I::S - 1) || bb < NBL) {
+#pragma unroll
+                        for (int r = 0; r < RL; ++r) srow[bb + r * NBL] = v[q * RL + r];
+                    }
+                }
+            } else if constexpr (MODE == kStoreMap) {
 #pragma unroll
                 for (int q = 0; q < I::bpt(I::S - 1); ++q) {
                     const int bb = t + q * C::T;
@@ -579,7 +631,21 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                 }
             }
         }
+        if (bulk_out) {  // block-uniform
+            fence_proxy_async();
+            __syncthreads();
+            if (tid == 0) {
+                for (int j = 0; j < C::RPB; ++j) {
+                    const int yy = grp * C::RPB + j;
+                    if (yy < out_rows)
+                        tma_store_1d(out + (size_t)yy * out_pitch, qbase + b * C::QB + j * C::OROW,
+                                     (uint32_t)(W2 * 8), pol_stream);
+                }
+                bulk_commit();
+            }
+        }
     }
+    if (tid == 0) bulk_wait_all();
 }
 
 }  // namespace zf
