@@ -122,6 +122,13 @@ ZF_DEV void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "me
 // reads of them (a bulk store issued after a barrier).
 ZF_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// Programmatic dependent launch: let the next kernel of the stream start its
+// prologue while this one runs, and wait for the previous kernel's completion
+// (and the visibility of its memory) before touching data it produced or
+// still reads.  Both are no-ops for kernels launched without the attribute.
+ZF_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+ZF_DEV void pdl_wait_prerequisites() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // 8-byte store with an L2 eviction policy.
 ZF_DEV void st_hint(float2* p, float2 v, uint64_t pol) {
     asm volatile("st.global.L2::cache_hint.v2.f32 [%0], {%1, %2}, %3;" ::"l"(p), "f"(v.x),
@@ -175,6 +182,8 @@ inline void tma_store_1d(void* dst, const void* src, uint32_t bytes, uint64_t) {
     emu_check_store(dst, src, bytes);
     std::memcpy(dst, src, bytes);
 }
+inline void pdl_launch_dependents() {}
+inline void pdl_wait_prerequisites() {}
 inline void bulk_commit() {}
 inline void bulk_wait_read() {}
 inline void bulk_wait_all() {}

@@ -8,6 +8,7 @@
 // src/cuda/real_conv_2d_binding.cu:51-140): shapes other than the FFT size are
 // run-time values here.
 #include <mutex>
+#include <utility>
 
 #include "launch.h"
 #include "xcorr_kernels.cuh"
@@ -49,6 +50,25 @@ cudaError_t configure(Kern kernel, KernelState& st, int smem, int threads, int d
 
 inline int min_int(int a, int b) { return a < b ? a : b; }
 
+// Launch with programmatic stream serialization: the kernel may start while
+// the previous kernel of the stream finishes; it calls griddepcontrol.wait
+// before touching that kernel's data.
+template <class... KArgs, class... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, int threads, int smem, cudaStream_t s,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(threads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 template <int W2, int NZ>
 cudaError_t r2c_t(const float* tmpl, float2* R, const float2* tw, int h, int w, int r_pitch,
                   long long r_tstride, int ntemplates, float scale, int device, cudaStream_t s) {
@@ -62,8 +82,8 @@ cudaError_t r2c_t(const float* tmpl, float2* R, const float2* tw, int h, int w, 
     const int groups = (h + C::RPB - 1) / C::RPB;
     const int per_t = min_int(groups, (cap + ntemplates - 1) / ntemplates);
     dim3 grid(per_t > 0 ? per_t : 1, ntemplates);
-    kernel<<<grid, C::THREADS, C::SMEM, s>>>(tmpl, R, tw, h, w, r_pitch, r_tstride, scale);
-    return cudaGetLastError();
+    return launch_pdl(kernel, grid, C::THREADS, C::SMEM, s, tmpl, R, tw, h, w, r_pitch, r_tstride,
+                      scale);
 }
 
 template <int H, bool CONJ, int NZ>
@@ -77,9 +97,8 @@ cudaError_t col_t(float2* Q, const float2* R, int r_pitch, const float2* spec, c
     cudaError_t e = configure(kernel, st, C::SMEM, C::THREADS, device, &cap);
     if (e != cudaSuccess) return e;
     const int grid = min_int((W2 + 1 + C::FPB - 1) / C::FPB, cap);
-    kernel<<<grid, C::THREADS, C::SMEM, s>>>(Q, R, r_pitch, spec, tw, h, W2, store_rows,
-                                             discard_r ? 1 : 0, status);
-    return cudaGetLastError();
+    return launch_pdl(kernel, dim3(grid), C::THREADS, C::SMEM, s, Q, R, r_pitch, spec, tw, h, W2,
+                      store_rows, discard_r ? 1 : 0, status);
 }
 
 template <int W2, int MODE>
@@ -94,9 +113,8 @@ cudaError_t c2r_t(const CUtensorMap* qmap, float* out, int* arg, const float2* t
     if (e != cudaSuccess) return e;
     const int groups = (out_rows + C::RPB - 1) / C::RPB;
     const int grid = min_int(groups, cap);
-    kernel<<<grid, C::THREADS, C::SMEM, s>>>(*qmap, out, arg, tw, out_rows, out_cols, out_pitch,
-                                             tindex, reset, status);
-    return cudaGetLastError();
+    return launch_pdl(kernel, dim3(grid), C::THREADS, C::SMEM, s, *qmap, out, arg, tw, out_rows,
+                      out_cols, out_pitch, tindex, reset, status);
 }
 
 // The pruned starts (nz = 1, 2) are instantiated for sizes >= 1024, where

@@ -105,8 +105,11 @@ __global__ void __launch_bounds__(R2cCfg<W2>::THREADS)
     const float* tm = tmpl + (size_t)blockIdx.y * h * w;
     float2* Rt = R + (size_t)blockIdx.y * r_tstride;
 
+    pdl_launch_dependents();
     typename F::Twiddles tw;
     F::template load_twiddles<2 * W2>(tw, twW, t);
+    // R may still be read by the previous kernel of the stream.
+    pdl_wait_prerequisites();
 
     // Row groups cover rows [0, round_up(h, 2)): the padding row of an odd h
     // is written as zeros by the split pass below.
@@ -219,11 +222,14 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
     }
     __syncthreads();
 
+    pdl_launch_dependents();
     typename F::Twiddles twf;
     F::template load_twiddles<H>(twf, twH, t);
     constexpr bool kShare = plan_palindrome(H);
     typename I::Twiddles twi_own;
     if constexpr (!kShare) I::template load_twiddles<H>(twi_own, twH, t);
+    // R comes from the previous kernel; Q may still be read by the one before.
+    pdl_wait_prerequisites();
 
     const uint32_t r_bytes = (uint32_t)round_up(h, 2) * 8u;
     const int stride = gridDim.x * C::FPB;
@@ -420,10 +426,7 @@ struct C2rCfg {
     // buffers 16 banks apart keep the stage exchanges conflict free.
     static constexpr int XB = RPB == 2 ? round_up(spad_size(W2) - 8, 16) + 8 : xbuf_len(W2);
     static constexpr int BOXK = tma_box(W2);
-    // One Q tile; after the first stage has read it, the same buffer stages
-    // the block's output rows (row stride W2 + 8: rows 16 banks apart).
-    static constexpr int OROW = W2 + 8;
-    static constexpr int QB = round_up(cmax(W2 * RPB, OROW * RPB), 16);
+    static constexpr int QB = round_up(W2 * RPB, 16);  // one Q tile
     static constexpr int FLOATS = 2 * QB + RPB * XB;
     static constexpr int SMEM = FLOATS * 8 + 2 * 8;
 };
@@ -464,6 +467,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     }
     __syncthreads();
 
+    pdl_launch_dependents();
     typename I::Twiddles tw;
     I::template load_twiddles<2 * W2>(tw, twW, t);
     // Pre-pass twiddles w_W^-k for k = bb + r NB0: w^-bb (per butterfly, from
@@ -474,6 +478,8 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
         const int bb = t + q * C::T;
         wpre[q] = (I::even(0) || bb < NB0) ? c_conj(__ldg(twW + bb)) : c_make(1.f, 0.f);
     }
+    // Q comes from the previous kernel.
+    pdl_wait_prerequisites();
 
     const bool vec_ok = out_cols == 2 * W2 && (out_pitch % 2) == 0 &&
                         (reinterpret_cast<size_t>(out) % 8) == 0;
@@ -490,29 +496,21 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                         pol_keep);
     };
 
-    // Full-width maps leave through bulk stores of whole rows staged in
-    // shared memory (row starts are 16-byte aligned); cropped maps use
-    // per-thread stores.
-    const bool bulk_out = MODE == kStoreMap && vec_ok && (out_pitch % 4) == 0 &&
-                          (reinterpret_cast<size_t>(out) % 16) == 0;
+    // Output rows leave through per-thread stores: staging them for bulk
+    // stores needs one more block barrier per group, which cost more than the
+    // store-queue stalls it removed.
     int grp = blockIdx.x;
     if (tid == 0 && grp < ngroups) issue(0, grp);
     for (int it = 0; grp < ngroups; ++it, grp += gridDim.x) {
         const int b = it & 1;
         const uint32_t parity = (it >> 1) & 1;
         const bool more = grp + (int)gridDim.x < ngroups;
-        if (tid == 0 && more) {
-            // buffer b^1 staged the previous group's rows: their bulk stores
-            // must have read it before the next tile lands there
-            bulk_wait_read();
-            issue(b ^ 1, grp + gridDim.x);
-        }
+        if (tid == 0 && more) issue(b ^ 1, grp + gridDim.x);
         const bool ok = mbar_wait_bounded(&mbar[b], parity);
         if (__syncthreads_or(!ok)) {
             if (tid == 0) {
                 atomicExch(status, kStatusTimeout);
                 if (more) mbar_wait_bounded(&mbar[b ^ 1], ((it + 1) >> 1) & 1);
-                bulk_wait_all();
             }
             return;
         }
@@ -545,17 +543,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
         const int y = grp * C::RPB + g;
         if (y < out_rows) {
             float* orow = out + (size_t)y * out_pitch;
-            if (MODE == kStoreMap && bulk_out) {
-                float2* srow = qbase + b * C::QB + g * C::OROW;
-#pragma unroll
-                for (int q = 0; q < I::bpt(I::S - 1); ++q) {
-                    const int bb = t + q * C::T;
-                    if (I::even(I::S - 1) || bb < NBL) {
-#pragma unroll
-                        for (int r = 0; r < RL; ++r) srow[bb + r * NBL] = v[q * RL + r];
-                    }
-                }
-            } else if constexpr (MODE == kStoreMap) {
+            if constexpr (MODE == kStoreMap) {
 #pragma unroll
                 for (int q = 0; q < I::bpt(I::S - 1); ++q) {
                     const int bb = t + q * C::T;
@@ -631,21 +619,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                 }
             }
         }
-        if (bulk_out) {  // block-uniform
-            fence_proxy_async();
-            __syncthreads();
-            if (tid == 0) {
-                for (int j = 0; j < C::RPB; ++j) {
-                    const int yy = grp * C::RPB + j;
-                    if (yy < out_rows)
-                        tma_store_1d(out + (size_t)yy * out_pitch, qbase + b * C::QB + j * C::OROW,
-                                     (uint32_t)(W2 * 8), pol_stream);
-                }
-                bulk_commit();
-            }
-        }
     }
-    if (tid == 0) bulk_wait_all();
 }
 
 }  // namespace zf
