@@ -163,6 +163,20 @@ ZFFT_API int zfft_check_device_status(int device, void* stream, int* status);
  * ZFFT_ERROR_TIMEOUT.  For tests. */
 ZFFT_API int zfft_selftest_wait_timeout(int device, void* stream);
 
+/* Image spectrum in the layout conv_data takes: the 2D real FFT of the
+ * (fft_y, fft_x) float32 image (row-major, contiguous), unnormalised,
+ * transposed to (fft_x/2 + 1, fft_y) complex64, i.e. element (kx, ky) at
+ * kx * fft_y + ky.  Replaces the caller-side torch.fft.rfftn(image)
+ * .transpose(-2, -1) that the reference's users run before calling the
+ * operator (README.md:224-228; tests/test_real_conv_2d.py:89-90, :125-127);
+ * the reference has no entry point for it.  conv_data_bytes must be at least
+ * (fft_x/2 + 1) * fft_y * 8; conv_data needs 16-byte alignment.  Uses no
+ * other memory (the row transforms are staged in conv_data itself) and, like
+ * the calls above, runs asynchronously on `stream`. */
+ZFFT_API int zfft_image_spectrum(const float* image, int fft_size_y, int fft_size_x,
+                                 void* conv_data, size_t conv_data_bytes, int device,
+                                 void* stream);
+
 /* Library version as major * 10000 + minor * 100 + patch. */
 ZFFT_API int zfft_get_version(void);
 

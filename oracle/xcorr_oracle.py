@@ -32,13 +32,15 @@ import numpy as np
 _HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-def image_spectrum_T(image) -> np.ndarray:
-    """rfft2 of a real (H, W) image, transposed to (W/2+1, H), complex64.
+def image_spectrum_T(image, dtype=np.complex64) -> np.ndarray:
+    """rfft2 of a real (H, W) image, transposed to (W/2+1, H).
 
-    The layout zipFFT's operator expects for `conv_data` (README.md:224-228,
-    test:125-127).  Computed in float64 and rounded once."""
+    The layout zipFFT's operator expects for `conv_data`, which the reference's
+    callers compute as `torch.fft.rfftn(image).transpose(-2, -1)` (README.md:
+    224-228, test:89-90 and :125-127).  Computed in float64 and rounded once to
+    `dtype` (complex64 by default; complex128 keeps the float64 values)."""
     img = np.asarray(image, dtype=np.float64)
-    return np.ascontiguousarray(np.fft.rfft2(img).T).astype(np.complex64)
+    return np.ascontiguousarray(np.fft.rfft2(img).T).astype(dtype)
 
 
 def out_shape(h: int, w: int, H: int, W: int, full: bool) -> Tuple[int, int]:
@@ -145,9 +147,11 @@ def direct_corr2d(template, image, cross_correlate: bool = True, full: bool = Fa
 # Error metrics (tolerances of BASELINE north star and the reference test)
 # ---------------------------------------------------------------------------
 def rel_l2(ref, out) -> float:
-    """||ref - out|| / ||ref|| (test:173)."""
-    ref = np.asarray(ref, dtype=np.float64)
-    out = np.asarray(out, dtype=np.float64)
+    """||ref - out|| / ||ref|| (test:173); complex inputs keep both parts."""
+    cplx = np.iscomplexobj(ref) or np.iscomplexobj(out)
+    dt = np.complex128 if cplx else np.float64
+    ref = np.asarray(ref, dtype=dt)
+    out = np.asarray(out, dtype=dt)
     return float(np.linalg.norm(ref - out) / max(np.linalg.norm(ref), 1e-300))
 
 

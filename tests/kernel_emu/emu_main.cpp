@@ -7,12 +7,15 @@
 // oracle on small sizes before any of it runs on a GPU.  It is never part of
 // the library: the library has no CPU path.
 //
-// Usage: zf_emu <in.bin> <out.bin>
+// Usage: zf_emu <in.bin> <out.bin>, or zf_emu spectrum <in.bin> <out.bin>
 //   in.bin : int32 header {B, sy, sx, H, W, oy, ox, conj, grid_cap, nz_col,
 //            nz_row, chunk, max_mode}, float32 templates [B][sy][sx],
 //            complex64 spectrum [W/2+1][H]
 //   out.bin: float32 [B][oy][ox] maps, or with max_mode the float32 [oy][ox]
 //            running maximum and int32 [oy][ox] argmax over the templates
+// spectrum mode (zfft_image_spectrum's two launches):
+//   in.bin : int32 header {H, W, grid_cap}, float32 image [H][W]
+//   out.bin: complex64 [W/2+1][H]
 #include <atomic>
 #include <barrier>
 #include <cmath>
@@ -228,6 +231,14 @@ void run_r2c(const float* tm, float2* R, const float2* tw, int h, int w, int r_p
     emu_launch(dim3{(unsigned)per, (unsigned)nt, 1}, C::THREADS, C::SMEM, zf::k_row_r2c<W2, NZ>, tm,
                R, tw, h, w, r_pitch, r_tstride, sc);
 }
+template <int H>
+void run_col_fwd(float2* spec, const float2* tw, int W2, int cap) {
+    using C = zf::ColFwdCfg<H>;
+    int grid = (W2 + C::FPB - 1) / C::FPB;
+    if (grid > cap) grid = cap;
+    emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_col_fwd<H>, spec, tw, W2,
+               &g_status);
+}
 template <int W2>
 void run_c2r(const float2* Q, int H, float* out, int* arg, const float2* tw, int orows, int ocols,
              int tindex, int reset, int cap) {
@@ -287,7 +298,45 @@ static void c2r(int W, const float2* Q, int H, float* out, int* arg, const float
     std::exit(2);
 }
 
+static void col_fwd(int H, float2* spec, const float2* tw, int W2, int cap) {
+#define X(N) \
+    if (H == N) return run_col_fwd<N>(spec, tw, W2, cap);
+    EMU_SIZES(X)
+#undef X
+    std::fprintf(stderr, "unsupported H %d\n", H);
+    std::exit(2);
+}
+
+// The host sequence of zfft_image_spectrum: the unscaled row pass over all
+// image rows into the output (pitch H), then the in-place column pass.
+static int spectrum_main(const char* in, const char* outp) {
+    FILE* f = std::fopen(in, "rb");
+    if (!f) return 2;
+    int hd[3];
+    if (std::fread(hd, sizeof(int), 3, f) != 3) return 2;
+    const int H = hd[0], W = hd[1], cap = hd[2];
+    std::vector<float> img((size_t)H * W);
+    if (std::fread(img.data(), sizeof(float), img.size(), f) != img.size()) return 2;
+    std::fclose(f);
+    const size_t n = (size_t)(W / 2 + 1) * H;
+    std::vector<float4> store(n / 2 + 1);
+    float2* spec = reinterpret_cast<float2*>(store.data());
+    auto twH = twiddles(H), twW = twiddles(W);
+    r2c(W, 0, img.data(), spec, twW.data(), H, W, H, 0, 1, 1.0f, cap);
+    col_fwd(H, spec, twH.data(), W / 2, cap);
+    if (g_status != 0) {
+        std::fprintf(stderr, "device status %d\n", g_status);
+        return 3;
+    }
+    FILE* g = std::fopen(outp, "wb");
+    if (!g) return 2;
+    std::fwrite(spec, sizeof(float2), n, g);
+    std::fclose(g);
+    return 0;
+}
+
 int main(int argc, char** argv) {
+    if (argc == 4 && std::strcmp(argv[1], "spectrum") == 0) return spectrum_main(argv[2], argv[3]);
     if (argc != 3) {
         std::fprintf(stderr, "usage: zf_emu in.bin out.bin\n");
         return 2;

@@ -100,3 +100,22 @@ def test_built_library_matches_sources():
     from zipfft_b200 import build
 
     assert build.is_current(), "rebuild with python -m zipfft_b200.build"
+
+
+def test_image_spectrum_host_validation():
+    """zfft_image_spectrum rejects bad sizes and buffers before any device work."""
+    lib = _lib.load()
+    need = (64 // 2 + 1) * 128 * 8
+    assert lib.zfft_image_spectrum(None, 100, 64, None, need, 0, None) == _lib.ZFFT_ERROR_UNSUPPORTED
+    assert "Unsupported image size" in _lib.last_error()
+    assert lib.zfft_image_spectrum(None, 128, 64, None, need - 8, 0, None) == \
+        _lib.ZFFT_ERROR_INVALID_VALUE
+    assert "conv_data too small" in _lib.last_error()
+    assert lib.zfft_image_spectrum(None, 128, 64, None, need, 0, None) == \
+        _lib.ZFFT_ERROR_INVALID_VALUE
+    assert "null data pointer" in _lib.last_error()
+    buf = (ctypes.c_float * 64)()
+    base = ctypes.addressof(buf)
+    assert lib.zfft_image_spectrum(base + 2, 128, 64, (base + 15) // 16 * 16, need, 0, None) == \
+        _lib.ZFFT_ERROR_INVALID_VALUE
+    assert "misaligned" in _lib.last_error()

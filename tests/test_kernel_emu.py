@@ -116,3 +116,22 @@ def test_emulated_running_max_argmax(emu, tmp_path, chunk):
     (mv, av), refv = run_emu(emu, tmp_path, B, 12, 9, H, W, True, False, max_mode=True)
     assert mv.shape == (H - 11, W - 8)
     assert np.allclose(mv, refv.max(axis=0), rtol=0, atol=1e-5 * np.abs(refv).max())
+
+
+@pytest.mark.parametrize("H,W", [(64, 64), (128, 240), (240, 120), (2048, 64), (256, 512)])
+def test_emulated_image_spectrum(emu, tmp_path, H, W):
+    """zfft_image_spectrum's row and in-place column passes against the
+    float64 rfft2 (transposed), including the split of packed column 0 into
+    the kx = 0 and kx = W/2 rows."""
+    rng = np.random.default_rng(H + W)
+    img = rng.standard_normal((H, W)).astype(np.float32)
+    fin, fout = str(tmp_path / "in.bin"), str(tmp_path / "out.bin")
+    with open(fin, "wb") as f:
+        np.array([H, W, 3], np.int32).tofile(f)
+        img.tofile(f)
+    res = subprocess.run([emu, "spectrum", fin, fout], capture_output=True, text=True)
+    assert res.returncode == 0, res.stderr[-4000:]
+    out = np.fromfile(fout, np.complex64).reshape(W // 2 + 1, H)
+    ref = O.image_spectrum_T(img, dtype=np.complex128)
+    assert O.rel_l2(ref, out) < 1e-6
+    assert np.abs(out - ref).max() < 1e-5 * np.abs(ref).max()

@@ -33,6 +33,7 @@ SIGNATURES = {
                                               _c_int, _vp]),
     "zfft_pack_max_arg": (_c_int, [_vp, _vp, _vp, _c_size, _c_int, _vp]),
     "zfft_unpack_max_arg": (_c_int, [_vp, _vp, _vp, _c_size, _c_int, _vp]),
+    "zfft_image_spectrum": (_c_int, [_vp, _c_int, _c_int, _vp, _c_size, _c_int, _vp]),
     "zfft_workspace_bytes": (_c_size, [_c_int, _c_int]),
     "zfft_is_fft_size_supported": (_c_int, [_c_int]),
     "zfft_get_supported_conv_configs": (_c_int, [ctypes.POINTER(ctypes.c_int), _c_int]),

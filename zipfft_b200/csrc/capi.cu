@@ -195,6 +195,7 @@ using ColFn = cudaError_t (*)(float2*, const float2*, int, const float2*, const 
                               int, bool, int, bool, int*, int, cudaStream_t);
 using R2cFn = cudaError_t (*)(const float*, float2*, const float2*, int, int, int, long long, int,
                               float, int, int, cudaStream_t);
+using ColFwdFn = cudaError_t (*)(float2*, const float2*, int, int*, int, cudaStream_t);
 using QmapFn = cudaError_t (*)(const float2*, int, CUtensorMap*);
 using C2rFn = cudaError_t (*)(const CUtensorMap*, float*, int*, const float2*, int, int, int, int,
                               int, int*, int, cudaStream_t);
@@ -209,6 +210,13 @@ ColFn col_fn(int n) {
 R2cFn r2c_fn(int n) {
 #define ZF_X(N) \
     if (n == (N)) return zf::launch_row_r2c_##N;
+    ZF_FOR_EACH_FFT_SIZE(ZF_X)
+#undef ZF_X
+    return nullptr;
+}
+ColFwdFn col_fwd_fn(int n) {
+#define ZF_X(N) \
+    if (n == (N)) return zf::launch_col_fwd_##N;
     ZF_FOR_EACH_FFT_SIZE(ZF_X)
 #undef ZF_X
     return nullptr;
@@ -555,6 +563,49 @@ int zfft_stage_timing_read(double* ms, int* launches, int n) {
 }
 
 int zfft_get_version(void) { return kVersion; }
+
+int zfft_image_spectrum(const float* image, int fft_size_y, int fft_size_x, void* conv_data,
+                        size_t conv_data_bytes, int device, void* stream) {
+    g_last_error.clear();
+    const int H = fft_size_y, W = fft_size_x;
+    if (!supported(H) || !supported(W))
+        return fail(ZFFT_ERROR_UNSUPPORTED,
+                    "Unsupported image size (%d, %d) (FFT sizes must be one of 64..4096 powers "
+                    "of two or 120, 240, 480, 960, 1920, 3840)",
+                    H, W);
+    const size_t need = (size_t)(W / 2 + 1) * (size_t)H * sizeof(float2);
+    if (conv_data_bytes < need)
+        return fail(ZFFT_ERROR_INVALID_VALUE,
+                    "conv_data too small: %zu bytes, need %zu ((W/2+1, H) complex64).",
+                    conv_data_bytes, need);
+    if (!image || !conv_data) return fail(ZFFT_ERROR_INVALID_VALUE, "null data pointer");
+    if (!aligned(image, 4) || !aligned(conv_data, 16))
+        return fail(ZFFT_ERROR_INVALID_VALUE,
+                    "misaligned pointer: image needs 4-byte alignment, conv_data 16-byte "
+                    "alignment (TMA copies)");
+    int ndev = 0;
+    cudaError_t e = cudaGetDeviceCount(&ndev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+    if (device < 0 || device >= ndev || device >= kMaxDevices)
+        return fail(ZFFT_ERROR_INVALID_VALUE, "invalid device index %d (%d devices)", device, ndev);
+    DeviceGuard guard(device);
+    if (guard.err != cudaSuccess) return cuda_fail(guard.err, "cudaSetDevice");
+    int rc = ensure_device(device);
+    if (rc != ZFFT_SUCCESS) return rc;
+    const float2* pool = g_dev_pool[device];
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float2* spec = static_cast<float2*>(conv_data);
+    // Row pass: every image row (full width, nothing pruned), unscaled,
+    // column-major into the output itself (pitch H); then the column pass in
+    // place.
+    e = r2c_fn(W)(image, spec, pool + tw_offset(W), H, W, H, 0, 1, 1.0f, 0, device, s);
+    if (e != cudaSuccess) return cuda_fail(e, "row r2c launch");
+    if ((e = trace_sync(s, "k_row_r2c image", 0)) != cudaSuccess) return cuda_fail(e, "k_row_r2c");
+    e = col_fwd_fn(H)(spec, pool + tw_offset(H), W / 2, g_dev_status[device], device, s);
+    if (e != cudaSuccess) return cuda_fail(e, "column launch");
+    if ((e = trace_sync(s, "k_col_fwd", 0)) != cudaSuccess) return cuda_fail(e, "k_col_fwd");
+    return ZFFT_SUCCESS;
+}
 
 int zfft_padded_real_corr_2d_max(const float* input, int batch, int signal_y, int signal_x,
                                  void* fft_workspace, size_t fft_workspace_bytes,

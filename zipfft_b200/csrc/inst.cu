@@ -101,6 +101,19 @@ cudaError_t col_t(float2* Q, const float2* R, int r_pitch, const float2* spec, c
                       store_rows, discard_r ? 1 : 0, status);
 }
 
+template <int H>
+cudaError_t col_fwd_t(float2* spec, const float2* tw, int W2, int* status, int device,
+                      cudaStream_t s) {
+    using C = ColFwdCfg<H>;
+    static KernelState st;
+    auto kernel = k_col_fwd<H>;
+    int cap = 0;
+    cudaError_t e = configure(kernel, st, C::SMEM, C::THREADS, device, &cap);
+    if (e != cudaSuccess) return e;
+    const int grid = min_int((W2 + C::FPB - 1) / C::FPB, cap);
+    return launch_pdl(kernel, dim3(grid), C::THREADS, C::SMEM, s, spec, tw, W2, status);
+}
+
 template <int W2, int MODE>
 cudaError_t c2r_t(const CUtensorMap* qmap, float* out, int* arg, const float2* tw, int out_rows,
                   int out_cols, int out_pitch, int tindex, int reset, int* status, int device,
@@ -151,6 +164,11 @@ cudaError_t ZF_CAT(launch_col_, ZF_SIZE)(float2* Q, const float2* R, int r_pitch
     }
     return conj ? ZF_COL(true, 0) : ZF_COL(false, 0);
 #undef ZF_COL
+}
+
+cudaError_t ZF_CAT(launch_col_fwd_, ZF_SIZE)(float2* spec, const float2* tw, int W2, int* status,
+                                             int device, cudaStream_t s) {
+    return col_fwd_t<ZF_SIZE>(spec, tw, W2, status, device, s);
 }
 
 cudaError_t ZF_CAT(make_qmap_, ZF_SIZE)(const float2* Q, int H, CUtensorMap* map) {

@@ -399,6 +399,135 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
 }
 
 // ===========================================================================
+// Image spectrum, column pass (the operator's callers compute the spectrum as
+// rfftn(image).transpose(-2, -1): zipFFT README.md:224-228, test:89-90).  The
+// row kernel has written the image rows' real FFTs column-major into the
+// (W/2+1, H) output itself -- packed column kx in [0, W2), element (kx, y) at
+// kx * H + y -- and this kernel replaces each column by its forward H-point
+// FFT, in place: a column is read (by TMA) and rewritten only by the block
+// that owns it.  Packed column 0 holds P = X[., 0] + i X[., W/2] of two real
+// columns, whose spectra separate as
+//   S[0][k]    = (P^[k] + conj P^[-k]) / 2,
+//   S[W/2][k]  = (P^[k] - conj P^[-k]) / 2i,
+// the second into row W2 of the output, which no block reads.
+// ===========================================================================
+template <int H>
+struct ColFwdCfg {
+    static constexpr int T = fft_threads(H);
+    static constexpr int FPB = T >= 128 ? 1 : 128 / T;  // columns per block
+    static constexpr int THREADS = FPB * T;
+    static constexpr int MINB = cmax(1, 512 / THREADS);
+    static constexpr int XB = xbuf_len(H);
+    static constexpr int CB = round_up(H, 16);  // one input column
+    static constexpr int FLOATS = FPB * (XB + 2 * CB);
+    static constexpr int SMEM = FLOATS * 8 + 2 * 8;  // + two mbarriers
+};
+
+template <int H>
+__global__ void __launch_bounds__(ColFwdCfg<H>::THREADS, ColFwdCfg<H>::MINB)
+    k_col_fwd(float2* __restrict__ spec, const float2* __restrict__ twH, int W2,
+              int* __restrict__ status) {
+    using C = ColFwdCfg<H>;
+    using F = Stockham<H, C::T, false, false>;
+    static_assert(F::S >= 2, "column FFT needs at least two stages");
+    constexpr int RL = F::radix(F::S - 1), NBL = F::nbf(F::S - 1);
+
+    const int tid = threadIdx.x;
+    const int g = tid / C::T, t = tid % C::T;
+    float2* smem = dyn_smem();
+    float2* xbuf = smem + g * C::XB;
+    float2* cbase = smem + C::FPB * C::XB;  // [2][FPB][CB]
+    uint64_t* mbar = reinterpret_cast<uint64_t*>(cbase + 2 * C::FPB * C::CB);
+
+    // Groups past the last column transform stale buffers: start them at zero.
+    for (int i = tid; i < 2 * C::FPB * C::CB; i += C::THREADS) cbase[i] = c_make(0.f, 0.f);
+    __syncthreads();
+    if (tid == 0) {
+        mbar_init(&mbar[0], 1);
+        mbar_init(&mbar[1], 1);
+        mbar_init_fence();
+    }
+    __syncthreads();
+
+    pdl_launch_dependents();
+    typename F::Twiddles tw;
+    F::template load_twiddles<H>(tw, twH, t);
+    // The row pass over the image wrote the columns.
+    pdl_wait_prerequisites();
+
+    const int stride = gridDim.x * C::FPB;
+    const uint64_t pol_stream = l2_evict_first();
+    auto issue = [&](int b, int c0) {
+        uint32_t bytes = 0;
+        for (int j = 0; j < C::FPB; ++j)
+            if (c0 + j < W2) bytes += H * 8u;
+        mbar_arrive_expect_tx(&mbar[b], bytes);
+        for (int j = 0; j < C::FPB && c0 + j < W2; ++j)
+            tma_load_1d(cbase + (b * C::FPB + j) * C::CB, spec + (size_t)(c0 + j) * H, H * 8u,
+                        &mbar[b], pol_stream);
+    };
+
+    int c0 = blockIdx.x * C::FPB;
+    if (tid == 0 && c0 < W2) issue(0, c0);
+    for (int it = 0; c0 < W2; ++it, c0 += stride) {
+        const int b = it & 1;
+        const uint32_t parity = (it >> 1) & 1;
+        // The other buffer was last read before this iteration's barrier.
+        const bool more = c0 + stride < W2;
+        if (tid == 0 && more) issue(b ^ 1, c0 + stride);
+        const bool ok = mbar_wait_bounded(&mbar[b], parity);
+        // Also orders the previous iteration's reads of xbuf before this
+        // iteration's transform writes it.
+        if (__syncthreads_or(!ok)) {
+            if (tid == 0) {
+                atomicExch(status, kStatusTimeout);
+                if (more) mbar_wait_bounded(&mbar[b ^ 1], ((it + 1) >> 1) & 1);
+            }
+            return;
+        }
+
+        const int kx = c0 + g;
+        const float2* col = cbase + (b * C::FPB + g) * C::CB;
+        float2 v[F::MAXE];
+        auto ld = [&](int i) { return col[i]; };
+        F::template run_loader<0>(v, ld, xbuf, tw, t);
+
+        // Frequency k = bb + r * NBL sits in v[q * RL + r].
+        if (kx == 0) {
+#pragma unroll
+            for (int q = 0; q < F::bpt(F::S - 1); ++q) {
+                const int bb = t + q * C::T;
+                if (F::even(F::S - 1) || bb < NBL) {
+#pragma unroll
+                    for (int r = 0; r < RL; ++r) xbuf[bb + r * NBL] = v[q * RL + r];
+                }
+            }
+        } else if (kx < W2) {
+            float2* dst = spec + (size_t)kx * H;
+#pragma unroll
+            for (int q = 0; q < F::bpt(F::S - 1); ++q) {
+                const int bb = t + q * C::T;
+                if (F::even(F::S - 1) || bb < NBL) {
+#pragma unroll
+                    for (int r = 0; r < RL; ++r) dst[bb + r * NBL] = v[q * RL + r];
+                }
+            }
+        }
+        __syncthreads();
+        if (kx == 0) {  // split the packed column (its reads ended at the barrier above)
+            float2* s0 = spec;
+            float2* sn = spec + (size_t)W2 * H;
+            for (int k = t; k < H; k += C::T) {
+                const float2 p = xbuf[k];
+                const float2 m = xbuf[k == 0 ? 0 : H - k];
+                s0[k] = c_make(0.5f * (p.x + m.x), 0.5f * (p.y - m.y));
+                sn[k] = c_make(0.5f * (p.y + m.y), 0.5f * (m.x - p.x));
+            }
+        }
+    }
+}
+
+// ===========================================================================
 // Kernel 3: inverse real FFT of output rows: the split pre-pass
 //   2Z[k] = (X[k] + conj X[W2-k]) + i w^-k (X[k] - conj X[W2-k])
 // is fused into the reads of the first stage; a W2-point complex inverse FFT

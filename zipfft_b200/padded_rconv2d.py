@@ -26,8 +26,8 @@ import torch
 
 from . import _lib
 
-__all__ = ["corr", "conv", "corr_max", "get_supported_conv_configs", "supported_fft_sizes",
-           "workspace_bytes"]
+__all__ = ["corr", "conv", "corr_max", "image_spectrum", "get_supported_conv_configs",
+           "supported_fft_sizes", "workspace_bytes"]
 
 
 def _check(cond: bool, msg: str) -> None:
@@ -169,6 +169,39 @@ def corr_max(input: torch.Tensor, fft_workspace: torch.Tensor, conv_data: torch.
                                               int(fft_size_x), int(template_index_base),
                                               1 if reset else 0, device, stream)
     _lib.check(status)
+
+
+def image_spectrum(image: torch.Tensor, conv_data: torch.Tensor = None) -> torch.Tensor:
+    """The image spectrum that corr / conv take as conv_data:
+    rfftn(image).transpose(-2, -1), complex64 (W/2+1, H), computed on the GPU
+    by the library's own row and column kernels.  The reference leaves this to
+    the caller (README.md:224-228, tests/test_real_conv_2d.py:89-90).
+
+    image: float32 (H, W) contiguous CUDA tensor, H and W supported FFT sizes.
+    conv_data: optional complex64 (W/2+1, H) contiguous output on the same
+    device; allocated when omitted.  Returns conv_data."""
+    _check(image.is_cuda, "Image tensor must be on a CUDA device")
+    _check(image.dtype == torch.float32, "Image tensor must be of type torch.float32")
+    _check(image.dim() == 2, "Image tensor must be 2D (H, W)")
+    _check(image.is_contiguous(), "Image tensor must be contiguous")
+    H, W = image.shape
+    if conv_data is None:
+        conv_data = torch.empty(W // 2 + 1, H, dtype=torch.complex64, device=image.device)
+    _check(conv_data.dtype == torch.complex64,
+           "Convolution data tensor must be of type torch.complex64")
+    _check(conv_data.device == image.device,
+           "Convolution data tensor must be on the same device as the image tensor")
+    _check(tuple(conv_data.shape) == (W // 2 + 1, H),
+           f"Convolution data tensor must have shape ({W // 2 + 1}, {H}). "
+           f"Got {tuple(conv_data.shape)}.")
+    _check(conv_data.is_contiguous(), "Convolution data tensor must be contiguous")
+    lib = _lib.load()
+    device = image.device.index if image.device.index is not None else torch.cuda.current_device()
+    stream = torch.cuda.current_stream(device).cuda_stream
+    status = lib.zfft_image_spectrum(image.data_ptr(), H, W, conv_data.data_ptr(),
+                                     conv_data.numel() * conv_data.element_size(), device, stream)
+    _lib.check(status)
+    return conv_data
 
 
 def get_supported_conv_configs() -> List[Tuple[int, int, int, int, int, bool]]:
