@@ -84,17 +84,54 @@ def _cuda_unpack(keys: torch.Tensor, max_map: torch.Tensor, arg_map: torch.Tenso
 CUDA_OPS = SearchOps(_cuda_corr_max, _cuda_pack, _cuda_unpack, _cuda_workspace)
 
 
+@dataclass
+class SearchCheckpoint:
+    """One rank's progress through its shard: the running maps (host tensors)
+    after the templates of the shard before global index `next_index`.  A
+    search restarted with `resume=` continues from there; every rank resumes
+    from its own checkpoint (the maps are per rank until the final
+    reduction)."""
+
+    n_templates: int
+    rank: int
+    world: int
+    next_index: int
+    max_map: torch.Tensor
+    arg_map: torch.Tensor
+
+    def save(self, path: str) -> None:
+        torch.save({"n_templates": self.n_templates, "rank": self.rank, "world": self.world,
+                    "next_index": self.next_index, "max_map": self.max_map,
+                    "arg_map": self.arg_map}, path)
+
+    @staticmethod
+    def load(path: str) -> "SearchCheckpoint":
+        d = torch.load(path, map_location="cpu", weights_only=True)
+        return SearchCheckpoint(int(d["n_templates"]), int(d["rank"]), int(d["world"]),
+                                int(d["next_index"]), d["max_map"], d["arg_map"])
+
+
 def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y: int,
                     fft_size_x: int, *, batch_size: int = 256, full: bool = True,
                     group=None, device: Optional[torch.device] = None,
-                    ops: SearchOps = CUDA_OPS) -> Tuple[torch.Tensor, torch.Tensor]:
+                    ops: SearchOps = CUDA_OPS, checkpoint_every: int = 0,
+                    on_checkpoint: Optional[Callable[[SearchCheckpoint], None]] = None,
+                    resume: Optional[SearchCheckpoint] = None
+                    ) -> Tuple[torch.Tensor, torch.Tensor]:
     """Maximum and argmax (global template index) of the correlation per pixel.
 
     templates: (N, h, w) float32 -- the whole set (every rank passes the same
     tensor, on the host (pinned memory is fastest) or on its device); each rank
     correlates its contiguous shard.  conv_data: (W/2+1, H) complex64
     spectrum on this rank's device.  Returns (max_map float32, arg_map int32),
-    (H, W) if `full` else the valid crop, identical on every rank."""
+    (H, W) if `full` else the valid crop, identical on every rank.
+
+    Checkpoints: with checkpoint_every = k > 0, `on_checkpoint` receives a
+    SearchCheckpoint (maps copied to the host, which synchronises the device)
+    after every k-th batch of this rank's shard that leaves templates to do.
+    resume: a checkpoint of this rank from an earlier run of the same search
+    (same template count, rank and world size); the shard continues at its
+    next_index with its maps.  The result equals the uninterrupted search's."""
     import torch.distributed as dist
 
     distributed = dist.is_available() and dist.is_initialized()
@@ -106,8 +143,24 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
     oy, ox = (H, W) if full else (H - h + 1, W - w + 1)
     lo, hi = shard_range(N, rank, world)
 
-    max_map = torch.full((oy, ox), float("-inf"), dtype=torch.float32, device=dev)
-    arg_map = torch.full((oy, ox), -1, dtype=torch.int32, device=dev)
+    start = lo
+    if resume is not None:
+        if (resume.n_templates, resume.rank, resume.world) != (N, rank, world):
+            raise ValueError(
+                f"checkpoint of a different search: {resume.n_templates} templates, rank "
+                f"{resume.rank} of {resume.world}; this is {N} templates, rank {rank} of {world}")
+        if not lo <= resume.next_index <= hi:
+            raise ValueError(f"checkpoint index {resume.next_index} outside this rank's shard "
+                             f"[{lo}, {hi})")
+        if tuple(resume.max_map.shape) != (oy, ox) or tuple(resume.arg_map.shape) != (oy, ox):
+            raise ValueError(f"checkpoint maps are {tuple(resume.max_map.shape)}, the search's "
+                             f"are {(oy, ox)}")
+        start = resume.next_index
+        max_map = resume.max_map.to(device=dev, dtype=torch.float32, copy=True).contiguous()
+        arg_map = resume.arg_map.to(device=dev, dtype=torch.int32, copy=True).contiguous()
+    else:
+        max_map = torch.full((oy, ox), float("-inf"), dtype=torch.float32, device=dev)
+        arg_map = torch.full((oy, ox), -1, dtype=torch.int32, device=dev)
     nb = min(batch_size, max(hi - lo, 1))
     workspace = ops.workspace(H, W, h, dev)
 
@@ -133,8 +186,9 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
             buf.copy_(templates[b0:b1])
         return buf
 
-    first = True
-    for j, b0 in enumerate(range(lo, hi, nb)):
+    # A resumed shard has maps to fold into; a fresh one starts by overwriting.
+    first = start == lo
+    for j, b0 in enumerate(range(start, hi, nb)):
         b1 = min(b0 + nb, hi)
         batch = stage(j % 2, b0, b1)
         ops.corr_max(batch, workspace, conv_data, max_map, arg_map, H, W, b0, first)
@@ -143,6 +197,10 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
             ev = torch.cuda.Event()
             ev.record(compute)
             events[j % 2] = ev
+        if checkpoint_every > 0 and on_checkpoint is not None and (j + 1) % checkpoint_every == 0 \
+                and b1 < hi:
+            on_checkpoint(SearchCheckpoint(N, rank, world, b1, max_map.to("cpu", copy=True),
+                                           arg_map.to("cpu", copy=True)))
 
     if world > 1:
         keys = ops.pack(max_map, arg_map)
