@@ -91,6 +91,8 @@ CASES = [
     (4, 30, 30, 256, 256, True, True, 2, 2, 4),
     (2, 100, 20, 2048, 64, True, True, 1, None, 2),   # one column per block: bulk column stores
     (1, 129, 9, 2048, 64, False, False, 2, None, 0),  # valid crop, odd store length
+    (2, 10, 100, 64, 2048, True, True, None, None, 2),  # rows on their own warps, named barriers
+    (1, 33, 300, 128, 2048, False, False, None, None, 0),
 ]
 
 
@@ -102,10 +104,10 @@ def test_emulated_kernels_match_oracle(emu, tmp_path, case):
     assert O.max_abs_over_peak(ref, out) < 1e-5
 
 
-@pytest.mark.parametrize("chunk", [0, 2])
-def test_emulated_running_max_argmax(emu, tmp_path, chunk):
+@pytest.mark.parametrize("chunk,W", [(0, 128), (2, 128), (0, 2048)])
+def test_emulated_running_max_argmax(emu, tmp_path, chunk, W):
     """The max / argmax epilogue of the inverse row pass."""
-    B, H, W = 5, 64, 128
+    B, H = 5, 64
     (mx, am), ref = run_emu(emu, tmp_path, B, 12, 9, H, W, True, True, chunk=chunk, max_mode=True)
     assert np.allclose(mx, ref.max(axis=0), rtol=0, atol=1e-5 * np.abs(ref).max())
     order = np.sort(ref, axis=0)
