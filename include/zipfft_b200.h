@@ -90,6 +90,20 @@ ZFFT_API int zfft_padded_real_corr_2d_max(const float* input, int batch, int sig
                                           int template_index_base, int reset, int device,
                                           void* stream);
 
+/* zfft_padded_real_corr_2d_max that also accumulates, per pixel, the sum and
+ * the sum of squares of the correlations over the templates (float32 maps of
+ * the same shape; reset overwrites them with the first template's values):
+ * the statistics 2D template matching normalises its scores with.  No
+ * counterpart in the reference (README.md:24 motivates the use). */
+ZFFT_API int zfft_padded_real_corr_2d_max_stats(const float* input, int batch, int signal_y,
+                                                int signal_x, void* fft_workspace,
+                                                size_t fft_workspace_bytes, const void* conv_data,
+                                                float* max_map, int32_t* arg_map, float* sum_map,
+                                                float* sumsq_map, int output_y, int output_x,
+                                                int fft_size_y, int fft_size_x,
+                                                int template_index_base, int reset, int device,
+                                                void* stream);
+
 /* (max, argmax) pairs <-> one int64 key each, ordered so that a single
  * integer MAX reduction across GPUs (e.g. ncclAllReduce with ncclInt64 /
  * ncclMax) yields the global maximum and, on ties, the lowest index.  n

@@ -12,7 +12,9 @@
 //            nz_row, chunk, max_mode}, float32 templates [B][sy][sx],
 //            complex64 spectrum [W/2+1][H]
 //   out.bin: float32 [B][oy][ox] maps, or with max_mode the float32 [oy][ox]
-//            running maximum and int32 [oy][ox] argmax over the templates
+//            running maximum and int32 [oy][ox] argmax over the templates,
+//            followed with max_mode 2 by the float32 [oy][ox] sum and sum of
+//            squares
 // spectrum mode (zfft_image_spectrum's two launches):
 //   in.bin : int32 header {H, W, grid_cap}, float32 image [H][W]
 //   out.bin: complex64 [W/2+1][H]
@@ -240,19 +242,25 @@ void run_col_fwd(float2* spec, const float2* tw, int W2, int cap) {
                &g_status);
 }
 template <int W2>
-void run_c2r(const float2* Q, int H, float* out, int* arg, const float2* tw, int orows, int ocols,
-             int tindex, int reset, int cap) {
+void run_c2r(const float2* Q, int H, float* out, int* arg, float* sum, float* sumsq,
+             const float2* tw, int orows, int ocols, int tindex, int reset, int cap) {
     using C = zf::C2rCfg<W2>;
     zf::CUtensorMap map{reinterpret_cast<const unsigned char*>(Q), H, W2, (long long)H * 8,
                         C::RPB, C::BOXK, 8};
     int groups = (orows + C::RPB - 1) / C::RPB;
     int grid = groups < cap ? groups : cap;
-    if (arg)
+    if (arg && sum)
+        emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM,
+                   zf::k_row_c2r<W2, zf::kRunningStats>, map, out, arg, sum, sumsq, tw, orows, ocols,
+                   ocols, tindex, reset, &g_status);
+    else if (arg)
         emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_row_c2r<W2, zf::kRunningMax>,
-                   map, out, arg, tw, orows, ocols, ocols, tindex, reset, &g_status);
+                   map, out, arg, (float*)nullptr, (float*)nullptr, tw, orows, ocols, ocols, tindex,
+                   reset, &g_status);
     else
         emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_row_c2r<W2, zf::kStoreMap>,
-                   map, out, (int*)nullptr, tw, orows, ocols, ocols, 0, 0, &g_status);
+                   map, out, (int*)nullptr, (float*)nullptr, (float*)nullptr, tw, orows, ocols, ocols,
+                   0, 0, &g_status);
 }
 
 #define EMU_SIZES(X) X(64) X(128) X(256) X(512) X(2048) X(120) X(240)
@@ -288,10 +296,11 @@ static void r2c(int W, int nz, const float* tm, float2* R, const float2* tw, int
     std::fprintf(stderr, "unsupported W %d\n", W);
     std::exit(2);
 }
-static void c2r(int W, const float2* Q, int H, float* out, int* arg, const float2* tw, int orows,
-                int ocols, int tindex, int reset, int cap) {
-#define X(N) \
-    if (W == N) return run_c2r<N / 2>(Q, H, out, arg, tw, orows, ocols, tindex, reset, cap);
+static void c2r(int W, const float2* Q, int H, float* out, int* arg, float* sum, float* sumsq,
+                const float2* tw, int orows, int ocols, int tindex, int reset, int cap) {
+#define X(N)                                                                                   \
+    if (W == N)                                                                                \
+        return run_c2r<N / 2>(Q, H, out, arg, sum, sumsq, tw, orows, ocols, tindex, reset, cap);
     EMU_SIZES(X)
 #undef X
     std::fprintf(stderr, "unsupported W %d\n", W);
@@ -349,6 +358,7 @@ int main(int argc, char** argv) {
     const bool conj = hd[7] != 0;
     const int cap = hd[8], nz_col = hd[9], nz_row = hd[10], chunk = hd[11];
     const bool max_mode = hd[12] != 0;  // fold into running max / argmax maps
+    const bool stats = hd[12] == 2;     // ... and into sum / sum-of-squares maps
     const int W2 = W / 2;
     std::vector<float> tm((size_t)B * sy * sx);
     std::vector<float2> spec((size_t)(W2 + 1) * H);
@@ -366,6 +376,9 @@ int main(int argc, char** argv) {
     float2* Rregion = Q + q_elems;
     std::vector<float> out((size_t)(max_mode ? 1 : B) * oy * ox);
     std::vector<int> arg(max_mode ? (size_t)oy * ox : 0);
+    std::vector<float> sum(stats ? (size_t)oy * ox : 0), sumsq(stats ? (size_t)oy * ox : 0);
+    float* sum_p = stats ? sum.data() : nullptr;
+    float* sumsq_p = stats ? sumsq.data() : nullptr;
     auto twH = twiddles(H), twW = twiddles(W);
     const float scale = float(1.0 / (double(H) * double(W)));
     const int step = chunk > 0 ? chunk : 1;
@@ -386,9 +399,11 @@ int main(int argc, char** argv) {
             }
             col(H, conj, nz_col, Q, Rt, rp, spec.data(), twH.data(), sy, W2, oy, cap);
             if (max_mode)
-                c2r(W, Q, H, out.data(), arg.data(), twW.data(), oy, ox, t, t == 0, cap);
+                c2r(W, Q, H, out.data(), arg.data(), sum_p, sumsq_p, twW.data(), oy, ox, t, t == 0,
+                    cap);
             else
-                c2r(W, Q, H, out.data() + (size_t)t * oy * ox, nullptr, twW.data(), oy, ox, 0, 0, cap);
+                c2r(W, Q, H, out.data() + (size_t)t * oy * ox, nullptr, nullptr, nullptr,
+                    twW.data(), oy, ox, 0, 0, cap);
         }
     }
     if (g_status != 0) {
@@ -399,6 +414,10 @@ int main(int argc, char** argv) {
     if (!g) return 2;
     std::fwrite(out.data(), sizeof(float), out.size(), g);
     if (max_mode) std::fwrite(arg.data(), sizeof(int), arg.size(), g);
+    if (stats) {
+        std::fwrite(sum.data(), sizeof(float), sum.size(), g);
+        std::fwrite(sumsq.data(), sizeof(float), sumsq.size(), g);
+    }
     std::fclose(g);
     return 0;
 }

@@ -11,16 +11,22 @@ from oracle import xcorr_oracle as O
 from zipfft_b200.search import SearchOps
 
 
-def corr_max(batch, workspace, conv_data, max_map, arg_map, H, W, base, reset):
+def corr_max(batch, workspace, conv_data, max_map, arg_map, H, W, base, reset, sum_map=None,
+             sumsq_map=None):
     full = tuple(max_map.shape) == (H, W)
     res = O.padded_corr2d_f64(batch.numpy(), conv_data.numpy(), H, W, True, full)
     mx = max_map.numpy()
     am = arg_map.numpy()
     for t in range(res.shape[0]):
         v = res[t].astype(np.float32)
-        upd = np.ones_like(mx, bool) if (reset and t == 0) else (v > mx)
+        first = reset and t == 0
+        upd = np.ones_like(mx, bool) if first else (v > mx)
         mx[upd] = v[upd]
         am[upd] = base + t
+        if sum_map is not None:  # float32 accumulation, as on the GPU
+            s, q = sum_map.numpy(), sumsq_map.numpy()
+            s[...] = v if first else s + v
+            q[...] = v * v if first else q + v * v
 
 
 def pack(max_map, arg_map):

@@ -65,8 +65,13 @@ def run_emu(exe, tmp_path, B, sy, sx, H, W, conj, full, nz_col=None, nz_row=None
     ref = O.padded_corr2d_f64(tm, spec, H, W, conj, full)
     if max_mode:
         raw = np.fromfile(fout, np.uint8)
-        mx = raw[: oy * ox * 4].view(np.float32).reshape(oy, ox)
-        am = raw[oy * ox * 4:].view(np.int32).reshape(oy, ox)
+        n = oy * ox * 4
+        mx = raw[:n].view(np.float32).reshape(oy, ox)
+        am = raw[n:2 * n].view(np.int32).reshape(oy, ox)
+        if max_mode == 2:
+            sm = raw[2 * n:3 * n].view(np.float32).reshape(oy, ox)
+            sq = raw[3 * n:4 * n].view(np.float32).reshape(oy, ox)
+            return (mx, am, sm, sq), ref
         return (mx, am), ref
     out = np.fromfile(fout, np.float32).reshape(B, oy, ox)
     return out, ref
@@ -137,3 +142,15 @@ def test_emulated_image_spectrum(emu, tmp_path, H, W):
     ref = O.image_spectrum_T(img, dtype=np.complex128)
     assert O.rel_l2(ref, out) < 1e-6
     assert np.abs(out - ref).max() < 1e-5 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("chunk,W,full", [(0, 128, True), (2, 2048, False)])
+def test_emulated_running_stats(emu, tmp_path, chunk, W, full):
+    """The max / argmax epilogue with per-pixel sum and sum of squares."""
+    B, H = 5, 64
+    (mx, am, sm, sq), ref = run_emu(emu, tmp_path, B, 12, 9, H, W, True, full, chunk=chunk,
+                                    max_mode=2)
+    peak = np.abs(ref).max()
+    assert np.allclose(mx, ref.max(axis=0), rtol=0, atol=1e-5 * peak)
+    assert O.rel_l2(ref.sum(axis=0), sm) < 1e-5
+    assert O.rel_l2((ref ** 2).sum(axis=0), sq) < 1e-5

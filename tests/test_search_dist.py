@@ -60,10 +60,12 @@ def _worker(rank, world, port, dup, fail_rank, out_dir):
         if rank == fail_rank:
             raise RuntimeError("injected failure before the reduction")
         tm, spec = _inputs(dup=dup)
-        mx, am = template_search(tm, spec, 32, 32, batch_size=2, full=True,
-                                 device=torch.device("cpu"), ops=CPU_OPS)
+        mx, am, sm, sq = template_search(tm, spec, 32, 32, batch_size=2, full=True,
+                                         device=torch.device("cpu"), ops=CPU_OPS, stats=True)
         np.save(os.path.join(out_dir, f"max{rank}.npy"), mx.numpy())
         np.save(os.path.join(out_dir, f"arg{rank}.npy"), am.numpy())
+        np.save(os.path.join(out_dir, f"sum{rank}.npy"), sm.numpy())
+        np.save(os.path.join(out_dir, f"sumsq{rank}.npy"), sq.numpy())
     finally:
         dist.destroy_process_group()
 
@@ -88,11 +90,19 @@ def test_two_rank_search_matches_single_process(tmp_path, dup):
         p.join(timeout=120)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     ref_max, ref_arg = _reference(dup)
+    from oracle import xcorr_oracle as O
+
+    tm, spec = _inputs(dup=dup)
+    res = O.padded_corr2d_f64(tm.numpy(), spec.numpy(), 32, 32, True, True)
     for r in range(2):
         mx = np.load(tmp_path / f"max{r}.npy")
         am = np.load(tmp_path / f"arg{r}.npy")
         assert np.array_equal(mx, ref_max)
         assert np.array_equal(am, ref_arg)  # ties (dup) keep the lower index, 1 not 4
+        # per-rank float32 partial sums, summed by the SUM all-reduce
+        assert O.rel_l2(res.sum(axis=0), np.load(tmp_path / f"sum{r}.npy")) < 1e-6
+        assert O.rel_l2((res ** 2).sum(axis=0), np.load(tmp_path / f"sumsq{r}.npy")) < 1e-6
+    assert np.array_equal(np.load(tmp_path / "sum0.npy"), np.load(tmp_path / "sum1.npy"))
     if dup is not None:
         assert not np.any(np.load(tmp_path / "arg0.npy") == dup[1])
 

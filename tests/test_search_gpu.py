@@ -59,6 +59,55 @@ def test_corr_max_in_batches_equals_one_call():
     assert torch.equal(mx1, mx2) and torch.equal(am1, am2)
 
 
+@pytest.mark.parametrize("B,h,w,H,W,full", [(6, 96, 96, 1024, 1024, True),
+                                            (5, 40, 30, 256, 512, False),
+                                            (3, 256, 256, 4096, 4096, True)])
+def test_corr_max_stats_match_oracle(B, h, w, H, W, full):
+    """Per-pixel sum and sum of squares over the templates, accumulated over
+    two calls (the first resets), next to the running max / argmax."""
+    import zipfft
+
+    _, tm, spec = make_inputs(B, h, w, H, W, seed=B + h + 1)
+    dev = torch.device("cuda", 0)
+    oy, ox = O.out_shape(h, w, H, W, full)
+    mx = torch.full((oy, ox), float("nan"), device=dev)
+    am = torch.full((oy, ox), -7, dtype=torch.int32, device=dev)
+    sm = torch.full((oy, ox), float("nan"), device=dev)
+    sq = torch.full((oy, ox), float("nan"), device=dev)
+    ws = torch.empty((B, H, W // 2 + 1), dtype=torch.complex64, device=dev)
+    tm_d, sp_d = tm.to(dev), spec.to(dev)
+    k = B // 2
+    zipfft.padded_rconv2d.corr_max(tm_d[:k], ws[:k], sp_d, mx, am, H, W, 0, True, sm, sq)
+    zipfft.padded_rconv2d.corr_max(tm_d[k:], ws[k:], sp_d, mx, am, H, W, k, False, sm, sq)
+    torch.cuda.synchronize()
+    ref = O.padded_corr2d_f64(tm.numpy(), spec.numpy(), H, W, True, full)
+    rmax, rarg, sure = maps(ref)
+    assert O.rel_l2(rmax, mx.cpu().numpy()) < 5e-6
+    assert np.array_equal(am.cpu().numpy()[sure], rarg[sure])
+    assert O.rel_l2(ref.sum(axis=0), sm.cpu().numpy()) < 5e-6
+    assert O.rel_l2((ref ** 2).sum(axis=0), sq.cpu().numpy()) < 5e-6
+    # the max / argmax maps are the same with and without the statistics
+    mx2, am2 = run_corr_max(tm, spec, H, W, full)
+    assert torch.equal(mx, mx2) and torch.equal(am, am2)
+
+
+def test_corr_max_stats_argument_errors():
+    import zipfft
+
+    _, tm, spec = make_inputs(2, 16, 16, 64, 64, seed=2)
+    dev = torch.device("cuda", 0)
+    mx = torch.empty((64, 64), device=dev)
+    am = torch.empty((64, 64), dtype=torch.int32, device=dev)
+    ws = torch.empty((2, 64, 33), dtype=torch.complex64, device=dev)
+    with pytest.raises(RuntimeError, match="given together"):
+        zipfft.padded_rconv2d.corr_max(tm.to(dev), ws, spec.to(dev), mx, am, 64, 64,
+                                       sum_map=torch.empty_like(mx))
+    with pytest.raises(RuntimeError, match="shape"):
+        zipfft.padded_rconv2d.corr_max(tm.to(dev), ws, spec.to(dev), mx, am, 64, 64,
+                                       sum_map=torch.empty((64, 63), device=dev),
+                                       sumsq_map=torch.empty_like(mx))
+
+
 def test_tie_keeps_lowest_index():
     _, tm, spec = make_inputs(4, 32, 32, 256, 256, seed=8)
     tm[3] = tm[1]  # identical templates: every pixel ties between 1 and 3
@@ -161,11 +210,13 @@ def test_search_two_gpus_nccl(tmp_path):
         "g = torch.Generator().manual_seed(3)\n"
         "img = torch.randn((512, 512), generator=g); tm = torch.randn((10, 40, 40), generator=g)\n"
         "spec = torch.from_numpy(O.image_spectrum_T(img.numpy())).cuda()\n"
-        "mx, am = template_search(tm, spec, 512, 512, batch_size=3)\n"
+        "mx, am, sm, sq = template_search(tm, spec, 512, 512, batch_size=3, stats=True)\n"
         "ref = O.padded_corr2d_f64(tm.numpy(), spec.cpu().numpy(), 512, 512, True, True)\n"
         "order = np.sort(ref, 0); sure = (order[-1] - order[-2]) > 1e-4 * np.abs(ref).max()\n"
         "ok = np.array_equal(am.cpu().numpy()[sure], ref.argmax(0)[sure]) and "
-        "O.rel_l2(ref.max(0), mx.cpu().numpy()) < 5e-6\n"
+        "O.rel_l2(ref.max(0), mx.cpu().numpy()) < 5e-6 and "
+        "O.rel_l2(ref.sum(0), sm.cpu().numpy()) < 5e-6 and "
+        "O.rel_l2((ref ** 2).sum(0), sq.cpu().numpy()) < 5e-6\n"
         "dist.destroy_process_group(); sys.exit(0 if ok else 1)\n")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
            "--master-addr=127.0.0.1", "--master-port=29517", str(script)]

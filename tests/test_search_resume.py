@@ -133,3 +133,29 @@ def test_two_rank_search_resumes_from_per_rank_checkpoints(tmp_path):
     for r in range(2):
         assert np.array_equal(np.load(tmp_path / f"max{r}.npy"), ref_max.numpy())
         assert np.array_equal(np.load(tmp_path / f"arg{r}.npy"), ref_arg.numpy())
+
+
+def test_stats_search_resumes_with_its_sums(tmp_path):
+    """stats=True: checkpoints carry the sum maps; a resumed search equals the
+    uninterrupted one, and a checkpoint without sums is refused."""
+    tm, spec = _inputs()
+    ref = _search(tm, spec, stats=True)
+    got = []
+
+    def save_then_stop(cp):
+        got.append(cp)
+        raise Preempted
+
+    with pytest.raises(Preempted):
+        _search(tm, spec, stats=True, checkpoint_every=2, on_checkpoint=save_then_stop)
+    path = str(tmp_path / "cp.pt")
+    got[0].save(path)
+    cp = SearchCheckpoint.load(path)
+    assert cp.sum_map is not None and cp.next_index == 4
+    out = _search(tm, spec, stats=True, resume=cp)
+    for a, b in zip(out, ref):
+        assert torch.equal(a, b)
+    plain = []
+    _search(tm, spec, checkpoint_every=2, on_checkpoint=plain.append)
+    with pytest.raises(ValueError, match="no sum maps"):
+        _search(tm, spec, stats=True, resume=plain[0])

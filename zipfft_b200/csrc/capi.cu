@@ -197,8 +197,8 @@ using R2cFn = cudaError_t (*)(const float*, float2*, const float2*, int, int, in
                               float, int, int, cudaStream_t);
 using ColFwdFn = cudaError_t (*)(float2*, const float2*, int, int*, int, cudaStream_t);
 using QmapFn = cudaError_t (*)(const float2*, int, CUtensorMap*);
-using C2rFn = cudaError_t (*)(const CUtensorMap*, float*, int*, const float2*, int, int, int, int,
-                              int, int*, int, cudaStream_t);
+using C2rFn = cudaError_t (*)(const CUtensorMap*, float*, int*, float*, float*, const float2*, int,
+                              int, int, int, int, int*, int, cudaStream_t);
 
 ColFn col_fn(int n) {
 #define ZF_X(N) \
@@ -273,10 +273,12 @@ const int kConfigs[][6] = {
 // One call of the correlation path.  arg == nullptr: output holds `batch`
 // maps of oy x ox.  Otherwise output / arg are the running max / argmax maps
 // (oy x ox) that every template folds into, template t with index
-// tindex_base + t; reset: the first template overwrites them.
+// tindex_base + t; reset: the first template overwrites them.  With sum (and
+// sumsq) also given, every template is added to those maps as well.
 int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes,
         const void* conv_data, float* output, int oy, int ox, int H, int W, bool conj,
-        int device, void* stream, int* arg = nullptr, int tindex_base = 0, bool reset = false) {
+        int device, void* stream, int* arg = nullptr, int tindex_base = 0, bool reset = false,
+        float* sum = nullptr, float* sumsq = nullptr) {
     g_last_error.clear();
     if (batch < 0) return fail(ZFFT_ERROR_INVALID_VALUE, "batch must be >= 0. Got %d.", batch);
     if (sy < 1 || sx < 1)
@@ -312,6 +314,8 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
     if (!input || !ws || !conv_data || !output)
         return fail(ZFFT_ERROR_INVALID_VALUE, "null data pointer");
     if (arg && !aligned(arg, 4)) return fail(ZFFT_ERROR_INVALID_VALUE, "misaligned argmax map");
+    if ((sum && !aligned(sum, 4)) || (sumsq && !aligned(sumsq, 4)))
+        return fail(ZFFT_ERROR_INVALID_VALUE, "misaligned sum map");
     if (!aligned(input, 4) || !aligned(output, 4) || !aligned(ws, 16) || !aligned(conv_data, 16))
         return fail(ZFFT_ERROR_INVALID_VALUE,
                     "misaligned pointer: input/output need 4-byte alignment, fft_workspace and "
@@ -400,11 +404,11 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
             if ((e = trace_sync(s, "k_col_fused", t)) != cudaSuccess) return cuda_fail(e, "k_col_fused");
             m = timer_mark(s);
             if (arg)
-                e = c2r(&qmap, output, arg, twW, oy, ox, ox, tindex_base + t, (reset && t == 0) ? 1 : 0,
-                        status, device, s);
+                e = c2r(&qmap, output, arg, sum, sumsq, twW, oy, ox, ox, tindex_base + t,
+                        (reset && t == 0) ? 1 : 0, status, device, s);
             else
-                e = c2r(&qmap, output + (size_t)t * oy * ox, nullptr, twW, oy, ox, ox, 0, 0, status,
-                        device, s);
+                e = c2r(&qmap, output + (size_t)t * oy * ox, nullptr, nullptr, nullptr, twW, oy, ox,
+                        ox, 0, 0, status, device, s);
             if (e != cudaSuccess) return cuda_fail(e, "row c2r launch");
             timer_close(2, m, s);
             if ((e = trace_sync(s, "k_row_c2r", t)) != cudaSuccess) return cuda_fail(e, "k_row_c2r");
@@ -618,6 +622,23 @@ int zfft_padded_real_corr_2d_max(const float* input, int batch, int signal_y, in
     return run(input, batch, signal_y, signal_x, fft_workspace, fft_workspace_bytes, conv_data,
                max_map, output_y, output_x, fft_size_y, fft_size_x, true, device, stream,
                reinterpret_cast<int*>(arg_map), template_index_base, reset != 0);
+}
+
+int zfft_padded_real_corr_2d_max_stats(const float* input, int batch, int signal_y,
+                                       int signal_x, void* fft_workspace,
+                                       size_t fft_workspace_bytes, const void* conv_data,
+                                       float* max_map, int32_t* arg_map, float* sum_map,
+                                       float* sumsq_map, int output_y, int output_x,
+                                       int fft_size_y, int fft_size_x, int template_index_base,
+                                       int reset, int device, void* stream) {
+    if ((!arg_map || !sum_map || !sumsq_map) && batch > 0)
+        return fail(ZFFT_ERROR_INVALID_VALUE, "null argmax, sum or sum-of-squares map");
+    if (template_index_base < 0 || (long long)template_index_base + batch > 0x7FFFFFFFLL)
+        return fail(ZFFT_ERROR_INVALID_VALUE, "template indices must lie in [0, 2^31 - 1)");
+    return run(input, batch, signal_y, signal_x, fft_workspace, fft_workspace_bytes, conv_data,
+               max_map, output_y, output_x, fft_size_y, fft_size_x, true, device, stream,
+               reinterpret_cast<int*>(arg_map), template_index_base, reset != 0, sum_map,
+               sumsq_map);
 }
 
 namespace {

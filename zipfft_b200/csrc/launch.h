@@ -21,7 +21,8 @@ namespace zf {
 // Row c2r: the Q tile map comes from make_qmap_<W> (same W); out_rows rows of
 // out_cols values at out_pitch.  arg == nullptr: store the map into out;
 // otherwise fold it into the running max (out) / argmax (arg) maps with
-// template index tindex (reset: overwrite instead of compare).
+// template index tindex (reset: overwrite instead of compare), and with sum
+// != nullptr also add it and its square to the sum / sumsq maps.
 #define ZF_DECL(N)                                                                              \
     cudaError_t launch_row_r2c_##N(const float* tmpl, float2* R, const float2* tw, int h, int w, \
                                    int r_pitch, long long r_tstride, int ntemplates, float scale, \
@@ -32,10 +33,10 @@ namespace zf {
     cudaError_t launch_col_fwd_##N(float2* spec, const float2* tw, int W2, int* status,         \
                                    int device, cudaStream_t s);                                  \
     cudaError_t make_qmap_##N(const float2* Q, int H, CUtensorMap* map);                        \
-    cudaError_t launch_row_c2r_##N(const CUtensorMap* qmap, float* out, int* arg,               \
-                                   const float2* tw, int out_rows, int out_cols, int out_pitch,  \
-                                   int tindex, int reset, int* status, int device,               \
-                                   cudaStream_t s);
+    cudaError_t launch_row_c2r_##N(const CUtensorMap* qmap, float* out, int* arg, float* sum,   \
+                                   float* sumsq, const float2* tw, int out_rows, int out_cols,   \
+                                   int out_pitch, int tindex, int reset, int* status,            \
+                                   int device, cudaStream_t s);
 ZF_FOR_EACH_FFT_SIZE(ZF_DECL)
 #undef ZF_DECL
 

@@ -563,18 +563,22 @@ struct C2rCfg {
 // Epilogues of the inverse row pass.
 constexpr int kStoreMap = 0;  // write the correlation map
 constexpr int kRunningMax = 1;  // fold it into a running per-pixel max / argmax
+constexpr int kRunningStats = 2;  // ... and into per-pixel sum and sum of squares
 
 // MODE kStoreMap: out[y][x] = correlation.  MODE kRunningMax: out is the
 // running maximum map and arg the template-index map (same pitch); where the
 // correlation is strictly greater than the stored maximum (or everywhere when
 // `reset`), the maximum becomes the correlation and the index `tindex`.
 // Templates folded in increasing index order therefore keep the lowest index
-// on ties.
+// on ties.  MODE kRunningStats: as kRunningMax, and the correlation and its
+// square are also added to the maps sum and sumsq (same pitch; `reset`
+// overwrites them instead).
 template <int W2, int MODE>
 __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     k_row_c2r(const __grid_constant__ CUtensorMap qmap, float* __restrict__ out,
-              int* __restrict__ arg, const float2* __restrict__ twW, int out_rows, int out_cols,
-              int out_pitch, int tindex, int reset, int* __restrict__ status) {
+              int* __restrict__ arg, float* __restrict__ sum, float* __restrict__ sumsq,
+              const float2* __restrict__ twW, int out_rows, int out_cols, int out_pitch,
+              int tindex, int reset, int* __restrict__ status) {
     using C = C2rCfg<W2>;
     using I = Stockham<W2, C::T, true, false>;
     static_assert(I::S >= 2, "row FFT needs at least two stages");
@@ -741,6 +745,59 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                                 if (u1 && 2 * m + 1 < out_cols) {
                                     orow[2 * m + 1] = z.y;
                                     arow[2 * m + 1] = tindex;
+                                }
+                            }
+                        }
+                    }
+                }
+                if constexpr (MODE == kRunningStats) {
+                    // Per-pixel sum and sum of squares (float accumulation);
+                    // a butterfly's RL values at a time: loads first, then stores.
+                    float* srow = sum + (size_t)y * out_pitch;
+                    float* qrow = sumsq + (size_t)y * out_pitch;
+#pragma unroll
+                    for (int q = 0; q < I::bpt(I::S - 1); ++q) {
+                        const int bb = t + q * C::T;
+                        if (I::even(I::S - 1) || bb < NBL) {
+                            float2 s1[RL], s2[RL];
+#pragma unroll
+                            for (int r = 0; r < RL; ++r) {
+                                const int m = bb + r * NBL;
+                                s1[r] = s2[r] = c_make(0.f, 0.f);
+                                if (!reset) {
+                                    if (vec_ok) {
+                                        s1[r] = reinterpret_cast<const float2*>(srow)[m];
+                                        s2[r] = reinterpret_cast<const float2*>(qrow)[m];
+                                    } else {
+                                        if (2 * m < out_cols) {
+                                            s1[r].x = srow[2 * m];
+                                            s2[r].x = qrow[2 * m];
+                                        }
+                                        if (2 * m + 1 < out_cols) {
+                                            s1[r].y = srow[2 * m + 1];
+                                            s2[r].y = qrow[2 * m + 1];
+                                        }
+                                    }
+                                }
+                            }
+#pragma unroll
+                            for (int r = 0; r < RL; ++r) {
+                                const int m = bb + r * NBL;
+                                const float2 z = v[q * RL + r];
+                                const float2 a = c_make(s1[r].x + z.x, s1[r].y + z.y);
+                                const float2 b2 = c_make(fmaf(z.x, z.x, s2[r].x), fmaf(z.y, z.y, s2[r].y));
+                                if (vec_ok) {
+                                    reinterpret_cast<float2*>(srow)[m] = a;
+                                    reinterpret_cast<float2*>(qrow)[m] = b2;
+                                } else {
+                                    if (2 * m < out_cols) {
+                                        srow[2 * m] = a.x;
+                                        qrow[2 * m] = b2.x;
+                                    }
+                                    if (2 * m + 1 < out_cols) {
+                                        srow[2 * m + 1] = a.y;
+                                        qrow[2 * m + 1] = b2.y;
+                                    }
                                 }
                             }
                         }

@@ -135,7 +135,8 @@ def conv(input: torch.Tensor, fft_workspace: torch.Tensor, conv_data: torch.Tens
 
 def corr_max(input: torch.Tensor, fft_workspace: torch.Tensor, conv_data: torch.Tensor,
              max_map: torch.Tensor, arg_map: torch.Tensor, fft_size_y: int, fft_size_x: int,
-             template_index_base: int = 0, reset: bool = False) -> None:
+             template_index_base: int = 0, reset: bool = False,
+             sum_map: torch.Tensor = None, sumsq_map: torch.Tensor = None) -> None:
     """Cross-correlate every template like `corr`, folding the results into
     running per-pixel maps instead of writing one map per template.
 
@@ -143,7 +144,10 @@ def corr_max(input: torch.Tensor, fft_workspace: torch.Tensor, conv_data: torch.
     the index of the template that produced it; template t of `input` has
     index template_index_base + t and ties keep the lower index.  Both maps
     are (H-h+1, W-w+1) or (H, W).  reset=True: this call's first template
-    overwrites the maps (no initialisation needed).  No counterpart in the
+    overwrites the maps (no initialisation needed).  With sum_map and
+    sumsq_map (float32, same shape) every correlation and its square are also
+    added to them per pixel (reset overwrites them too): the statistics 2D
+    template matching normalises its scores with.  No counterpart in the
     reference; the 2D template-matching search its README motivates."""
     _check(max_map.dtype == torch.float32, "Max map tensor must be of type torch.float32")
     _check(arg_map.dtype == torch.int32, "Argmax map tensor must be of type torch.int32")
@@ -152,6 +156,16 @@ def corr_max(input: torch.Tensor, fft_workspace: torch.Tensor, conv_data: torch.
     _check(max_map.device == input.device and arg_map.device == input.device,
            "Max and argmax maps must be on the same device as the input tensor")
     _check(max_map.is_contiguous() and arg_map.is_contiguous(), "Maps must be contiguous")
+    stats = sum_map is not None or sumsq_map is not None
+    if stats:
+        _check(sum_map is not None and sumsq_map is not None,
+               "Sum and sum-of-squares maps must be given together")
+        for name, m in (("Sum", sum_map), ("Sum-of-squares", sumsq_map)):
+            _check(m.dtype == torch.float32, f"{name} map tensor must be of type torch.float32")
+            _check(m.shape == max_map.shape, f"{name} map must have the max map's shape")
+            _check(m.device == input.device,
+                   f"{name} map must be on the same device as the input tensor")
+            _check(m.is_contiguous(), "Maps must be contiguous")
     lead = (input.size(0),) if input.dim() == 3 else ()
     # Validate everything else exactly as corr does, with a shape stand-in for
     # the per-template output.
@@ -162,12 +176,19 @@ def corr_max(input: torch.Tensor, fft_workspace: torch.Tensor, conv_data: torch.
     device = input.device.index if input.device.index is not None else torch.cuda.current_device()
     stream = torch.cuda.current_stream(device).cuda_stream
     ws_bytes = fft_workspace.numel() * fft_workspace.element_size()
-    status = lib.zfft_padded_real_corr_2d_max(input.data_ptr(), batch, sy, sx,
-                                              fft_workspace.data_ptr(), ws_bytes,
-                                              conv_data.data_ptr(), max_map.data_ptr(),
-                                              arg_map.data_ptr(), oy, ox, int(fft_size_y),
-                                              int(fft_size_x), int(template_index_base),
-                                              1 if reset else 0, device, stream)
+    if stats:
+        status = lib.zfft_padded_real_corr_2d_max_stats(
+            input.data_ptr(), batch, sy, sx, fft_workspace.data_ptr(), ws_bytes,
+            conv_data.data_ptr(), max_map.data_ptr(), arg_map.data_ptr(), sum_map.data_ptr(),
+            sumsq_map.data_ptr(), oy, ox, int(fft_size_y), int(fft_size_x),
+            int(template_index_base), 1 if reset else 0, device, stream)
+    else:
+        status = lib.zfft_padded_real_corr_2d_max(input.data_ptr(), batch, sy, sx,
+                                                  fft_workspace.data_ptr(), ws_bytes,
+                                                  conv_data.data_ptr(), max_map.data_ptr(),
+                                                  arg_map.data_ptr(), oy, ox, int(fft_size_y),
+                                                  int(fft_size_x), int(template_index_base),
+                                                  1 if reset else 0, device, stream)
     _lib.check(status)
 
 

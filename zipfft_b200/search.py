@@ -33,7 +33,8 @@ class SearchOps:
     """The per-GPU operations of the search (the CUDA library by default).
 
     corr_max(batch (n, h, w), workspace, conv_data, max_map, arg_map, H, W,
-             template_index_base, reset) folds n templates into the maps."""
+             template_index_base, reset, sum_map=None, sumsq_map=None) folds n
+    templates into the maps (and into the sum / sum-of-squares maps if given)."""
 
     corr_max: Callable
     pack: Callable       # (max_map, arg_map) -> int64 keys
@@ -54,14 +55,23 @@ def _cuda_workspace(H: int, W: int, h: int, device) -> torch.Tensor:
 
 
 def _cuda_corr_max(batch, workspace, conv_data, max_map, arg_map, H, W, template_index_base,
-                   reset) -> None:
+                   reset, sum_map=None, sumsq_map=None) -> None:
     n, h, w = batch.shape
     oy, ox = max_map.shape
     dev = batch.device.index
-    st = _lib.load().zfft_padded_real_corr_2d_max(
-        batch.data_ptr(), n, h, w, workspace.data_ptr(), workspace.numel() * 8,
-        conv_data.data_ptr(), max_map.data_ptr(), arg_map.data_ptr(), oy, ox, H, W,
-        int(template_index_base), 1 if reset else 0, dev, torch.cuda.current_stream(dev).cuda_stream)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    lib = _lib.load()
+    if sum_map is not None:
+        st = lib.zfft_padded_real_corr_2d_max_stats(
+            batch.data_ptr(), n, h, w, workspace.data_ptr(), workspace.numel() * 8,
+            conv_data.data_ptr(), max_map.data_ptr(), arg_map.data_ptr(), sum_map.data_ptr(),
+            sumsq_map.data_ptr(), oy, ox, H, W, int(template_index_base), 1 if reset else 0, dev,
+            stream)
+    else:
+        st = lib.zfft_padded_real_corr_2d_max(
+            batch.data_ptr(), n, h, w, workspace.data_ptr(), workspace.numel() * 8,
+            conv_data.data_ptr(), max_map.data_ptr(), arg_map.data_ptr(), oy, ox, H, W,
+            int(template_index_base), 1 if reset else 0, dev, stream)
     _lib.check(st)
 
 
@@ -98,17 +108,21 @@ class SearchCheckpoint:
     next_index: int
     max_map: torch.Tensor
     arg_map: torch.Tensor
+    sum_map: Optional[torch.Tensor] = None    # with stats=True
+    sumsq_map: Optional[torch.Tensor] = None
 
     def save(self, path: str) -> None:
         torch.save({"n_templates": self.n_templates, "rank": self.rank, "world": self.world,
                     "next_index": self.next_index, "max_map": self.max_map,
-                    "arg_map": self.arg_map}, path)
+                    "arg_map": self.arg_map, "sum_map": self.sum_map,
+                    "sumsq_map": self.sumsq_map}, path)
 
     @staticmethod
     def load(path: str) -> "SearchCheckpoint":
         d = torch.load(path, map_location="cpu", weights_only=True)
         return SearchCheckpoint(int(d["n_templates"]), int(d["rank"]), int(d["world"]),
-                                int(d["next_index"]), d["max_map"], d["arg_map"])
+                                int(d["next_index"]), d["max_map"], d["arg_map"],
+                                d.get("sum_map"), d.get("sumsq_map"))
 
 
 def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y: int,
@@ -116,8 +130,8 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
                     group=None, device: Optional[torch.device] = None,
                     ops: SearchOps = CUDA_OPS, checkpoint_every: int = 0,
                     on_checkpoint: Optional[Callable[[SearchCheckpoint], None]] = None,
-                    resume: Optional[SearchCheckpoint] = None
-                    ) -> Tuple[torch.Tensor, torch.Tensor]:
+                    resume: Optional[SearchCheckpoint] = None, stats: bool = False
+                    ) -> Tuple[torch.Tensor, ...]:
     """Maximum and argmax (global template index) of the correlation per pixel.
 
     templates: (N, h, w) float32 -- the whole set (every rank passes the same
@@ -131,7 +145,11 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
     after every k-th batch of this rank's shard that leaves templates to do.
     resume: a checkpoint of this rank from an earlier run of the same search
     (same template count, rank and world size); the shard continues at its
-    next_index with its maps.  The result equals the uninterrupted search's."""
+    next_index with its maps.  The result equals the uninterrupted search's.
+
+    stats=True: also the per-pixel sum and sum of squares of the correlations
+    over all templates (float32; summed across ranks with one all-reduce), for
+    z-score normalisation; returns (max_map, arg_map, sum_map, sumsq_map)."""
     import torch.distributed as dist
 
     distributed = dist.is_available() and dist.is_initialized()
@@ -155,12 +173,23 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
         if tuple(resume.max_map.shape) != (oy, ox) or tuple(resume.arg_map.shape) != (oy, ox):
             raise ValueError(f"checkpoint maps are {tuple(resume.max_map.shape)}, the search's "
                              f"are {(oy, ox)}")
+        if stats and (resume.sum_map is None or resume.sumsq_map is None):
+            raise ValueError("checkpoint has no sum maps; it comes from a search without stats")
         start = resume.next_index
         max_map = resume.max_map.to(device=dev, dtype=torch.float32, copy=True).contiguous()
         arg_map = resume.arg_map.to(device=dev, dtype=torch.int32, copy=True).contiguous()
     else:
         max_map = torch.full((oy, ox), float("-inf"), dtype=torch.float32, device=dev)
         arg_map = torch.full((oy, ox), -1, dtype=torch.int32, device=dev)
+    sum_map = sumsq_map = None
+    if stats:
+        if resume is not None:
+            sum_map = resume.sum_map.to(device=dev, dtype=torch.float32, copy=True).contiguous()
+            sumsq_map = resume.sumsq_map.to(device=dev, dtype=torch.float32,
+                                            copy=True).contiguous()
+        else:  # an empty shard contributes zeros
+            sum_map = torch.zeros((oy, ox), dtype=torch.float32, device=dev)
+            sumsq_map = torch.zeros((oy, ox), dtype=torch.float32, device=dev)
     nb = min(batch_size, max(hi - lo, 1))
     workspace = ops.workspace(H, W, h, dev)
 
@@ -191,7 +220,11 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
     for j, b0 in enumerate(range(start, hi, nb)):
         b1 = min(b0 + nb, hi)
         batch = stage(j % 2, b0, b1)
-        ops.corr_max(batch, workspace, conv_data, max_map, arg_map, H, W, b0, first)
+        if stats:
+            ops.corr_max(batch, workspace, conv_data, max_map, arg_map, H, W, b0, first,
+                         sum_map, sumsq_map)
+        else:
+            ops.corr_max(batch, workspace, conv_data, max_map, arg_map, H, W, b0, first)
         first = False
         if copy is not None:  # the buffer may be refilled once this batch's kernels ran
             ev = torch.cuda.Event()
@@ -199,11 +232,18 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
             events[j % 2] = ev
         if checkpoint_every > 0 and on_checkpoint is not None and (j + 1) % checkpoint_every == 0 \
                 and b1 < hi:
-            on_checkpoint(SearchCheckpoint(N, rank, world, b1, max_map.to("cpu", copy=True),
-                                           arg_map.to("cpu", copy=True)))
+            snap = (lambda m: None if m is None else m.to("cpu", copy=True))
+            on_checkpoint(SearchCheckpoint(N, rank, world, b1, snap(max_map), snap(arg_map),
+                                           snap(sum_map), snap(sumsq_map)))
 
     if world > 1:
         keys = ops.pack(max_map, arg_map)
         dist.all_reduce(keys, op=dist.ReduceOp.MAX, group=group)
         ops.unpack(keys, max_map, arg_map)
+        if stats:
+            both = torch.stack([sum_map, sumsq_map])
+            dist.all_reduce(both, op=dist.ReduceOp.SUM, group=group)
+            sum_map, sumsq_map = both[0], both[1]
+    if stats:
+        return max_map, arg_map, sum_map, sumsq_map
     return max_map, arg_map
