@@ -144,6 +144,18 @@ bool zf::emu_mbar_try_wait(uint64_t* bar, uint32_t parity) {
     std::lock_guard<std::mutex> l(emu_bar_mu);
     return emu_bars.at(bar).phase != parity;  // the phase with that parity completed
 }
+// Bulk L2 prefetch rule: 16-byte aligned address and size; the emulator
+// also reads the range, so ASan flags a prefetch outside any allocation.
+void zf::emu_check_prefetch(const void* p, uint32_t bytes) {
+    if (reinterpret_cast<uintptr_t>(p) % 16 || bytes % 16 || bytes == 0) {
+        std::fprintf(stderr, "bad L2 prefetch %p %u\n", p, bytes);
+        std::abort();
+    }
+    volatile unsigned char sink = 0;
+    const unsigned char* c = static_cast<const unsigned char*>(p);
+    sink = sink + c[0] + c[bytes - 1];
+    (void)sink;
+}
 // discard.global.L2 rule: whole 128-byte lines only.
 void zf::emu_discard_line(const void* p) {
     if (reinterpret_cast<uintptr_t>(p) % 128) {

@@ -141,6 +141,12 @@ ZF_DEV void st_hint(float* p, float v, uint64_t pol) {
 
 // Drop a 128-byte L2 line without writing it back (its data becomes
 // undefined).  `p` must be 128-byte aligned and no one may read the line again.
+// Prefetch `bytes` (a multiple of 16) at the 16-byte aligned global address
+// p into L2, asynchronously; nothing waits for it.
+ZF_DEV void l2_prefetch_bulk(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 ZF_DEV void l2_discard_line(const void* p) {
     asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory");
 }
@@ -190,6 +196,8 @@ inline void bulk_wait_all() {}
 inline void fence_proxy_async() {}
 inline void st_hint(float2* p, float2 v, uint64_t) { *p = v; }
 inline void st_hint(float* p, float v, uint64_t) { *p = v; }
+void emu_check_prefetch(const void* p, uint32_t bytes);
+inline void l2_prefetch_bulk(const void* p, uint32_t bytes) { emu_check_prefetch(p, bytes); }
 void emu_discard_line(const void* p);
 inline void l2_discard_line(const void* p) { emu_discard_line(p); }
 inline void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,

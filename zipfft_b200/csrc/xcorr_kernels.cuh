@@ -535,6 +535,13 @@ __global__ void __launch_bounds__(ColFwdCfg<H>::THREADS, ColFwdCfg<H>::MINB)
 // rows; a group's Q tile (all W2 columns x RPB rows) arrives by 2D TMA loads,
 // double-buffered.
 // ===========================================================================
+// L2 prefetch of the whole 16-byte chunks inside the n floats at p.
+ZF_DEV void prefetch_row(const float* p, int n) {
+    const size_t a = (reinterpret_cast<size_t>(p) + 15) & ~size_t(15);
+    const size_t e = reinterpret_cast<size_t>(p + n) & ~size_t(15);
+    if (e > a) l2_prefetch_bulk(reinterpret_cast<const void*>(a), (uint32_t)(e - a));
+}
+
 // Largest divisor of n not above 256 (the TMA box limit).
 constexpr int tma_box(int n) {
     for (int d = 256; d >= 1; --d)
@@ -639,6 +646,21 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
         const uint32_t parity = (it >> 1) & 1;
         const bool more = grp + (int)gridDim.x < ngroups;
         if (tid == 0 && more) issue(b ^ 1, grp + gridDim.x);
+        if constexpr (MODE != kStoreMap) {
+            // The maps this group's epilogue reads: into L2 while the group
+            // is transformed (whole 16-byte chunks inside each row only).
+            if (tid == 0) {
+                for (int r = 0; r < C::RPB; ++r) {
+                    const int yy = grp * C::RPB + r;
+                    if (yy >= out_rows) break;
+                    prefetch_row(out + (size_t)yy * out_pitch, out_cols);
+                    if constexpr (MODE == kRunningStats) {
+                        prefetch_row(sum + (size_t)yy * out_pitch, out_cols);
+                        prefetch_row(sumsq + (size_t)yy * out_pitch, out_cols);
+                    }
+                }
+            }
+        }
         const bool ok = mbar_wait_bounded(&mbar[b], parity);
         if (__syncthreads_or(!ok)) {
             if (tid == 0) {
