@@ -71,6 +71,17 @@ ZFFT_API int zfft_padded_real_conv_2d(const float* input, int batch, int signal_
                              const void* conv_data, float* output, int output_y, int output_x,
                              int fft_size_y, int fft_size_x, int device, void* stream);
 
+/* zfft_padded_real_corr_2d that also writes peaks[t] = the largest value of
+ * output map t (batch float32 values, computed by the kernel that writes the
+ * map, so no second pass over the output).  No counterpart in the reference;
+ * the per-template best score of 2D template matching. */
+ZFFT_API int zfft_padded_real_corr_2d_peaks(const float* input, int batch, int signal_y,
+                                            int signal_x, void* fft_workspace,
+                                            size_t fft_workspace_bytes, const void* conv_data,
+                                            float* output, int output_y, int output_x,
+                                            int fft_size_y, int fft_size_x, float* peaks,
+                                            int device, void* stream);
+
 /* 2D template matching's per-pixel search: cross-correlate every template
  * as zfft_padded_real_corr_2d does, but instead of writing one map per
  * template fold each correlation into running maps: max_map[y][x] keeps the

@@ -14,14 +14,16 @@
 //   out.bin: float32 [B][oy][ox] maps, or with max_mode the float32 [oy][ox]
 //            running maximum and int32 [oy][ox] argmax over the templates,
 //            followed with max_mode 2 by the float32 [oy][ox] sum and sum of
-//            squares
+//            squares; max_mode 3: the maps followed by float32 [B] peaks
 // spectrum mode (zfft_image_spectrum's two launches):
 //   in.bin : int32 header {H, W, grid_cap}, float32 image [H][W]
 //   out.bin: complex64 [W/2+1][H]
 #include <atomic>
 #include <barrier>
 #include <cmath>
+#include <algorithm>
 #include <map>
+#include <memory>
 #define INFINITY __builtin_inff()
 #include <mutex>
 #include <cstdio>
@@ -98,6 +100,26 @@ __attribute__((noinline)) int __syncthreads_or(int pred) {
     return r;
 }
 inline int atomicExch(int* p, int v) { return __atomic_exchange_n(p, v, __ATOMIC_SEQ_CST); }
+inline unsigned atomicMax(unsigned* p, unsigned v) {
+    unsigned cur = __atomic_load_n(p, __ATOMIC_SEQ_CST);
+    while (cur < v && !__atomic_compare_exchange_n(p, &cur, v, false, __ATOMIC_SEQ_CST,
+                                                   __ATOMIC_SEQ_CST)) {
+    }
+    return cur;
+}
+// Warp shuffles: every lane of the warp must call (full mask); each warp has
+// an exchange array and a barrier of its lanes.
+thread_local std::barrier<>* emu_warp_bar = nullptr;
+thread_local float* emu_warp_buf = nullptr;
+inline float __shfl_xor_sync(unsigned mask, float v, int lane_mask) {
+    if (mask != 0xffffffffu) std::abort();
+    const unsigned lane = threadIdx.x & 31u;
+    emu_warp_buf[lane] = v;
+    emu_warp_bar->arrive_and_wait();
+    const float r = emu_warp_buf[lane ^ (unsigned)lane_mask];
+    emu_warp_bar->arrive_and_wait();
+    return r;
+}
 template <class T>
 inline T __ldg(const T* p) {
     return *p;
@@ -191,6 +213,11 @@ void emu_launch(dim3 grid, int block, size_t smem_bytes, K kernel, A... args) {
     float2* smem = reinterpret_cast<float2*>((reinterpret_cast<uintptr_t>(store.data()) + 127) & ~uintptr_t(127));
     std::barrier<> bar(block);
     std::vector<void*> sites[2] = {std::vector<void*>(block), std::vector<void*>(block)};
+    const int nwarps = (block + 31) / 32;
+    std::vector<std::unique_ptr<std::barrier<>>> wbars;
+    for (int w = 0; w < nwarps; ++w)
+        wbars.push_back(std::make_unique<std::barrier<>>(std::min(32, block - 32 * w)));
+    std::vector<float> wbuf((size_t)nwarps * 32);
     std::vector<std::thread> threads;
     for (int tid = 0; tid < block; ++tid) {
         threads.emplace_back([&, tid] {
@@ -203,6 +230,8 @@ void emu_launch(dim3 grid, int block, size_t smem_bytes, K kernel, A... args) {
             emu_or_calls = 0;
             emu_bar_calls = 0;
             emu_sites = sites;
+            emu_warp_bar = wbars[tid / 32].get();
+            emu_warp_buf = wbuf.data() + (tid / 32) * 32;
             for (unsigned by = 0; by < grid.y; ++by) {
                 for (unsigned bx = 0; bx < grid.x; ++bx) {
                     blockIdx.x = bx;
@@ -255,24 +284,28 @@ void run_col_fwd(float2* spec, const float2* tw, int W2, int cap) {
 }
 template <int W2>
 void run_c2r(const float2* Q, int H, float* out, int* arg, float* sum, float* sumsq,
-             const float2* tw, int orows, int ocols, int tindex, int reset, int cap) {
+             unsigned* peak, const float2* tw, int orows, int ocols, int tindex, int reset,
+             int cap) {
     using C = zf::C2rCfg<W2>;
     zf::CUtensorMap map{reinterpret_cast<const unsigned char*>(Q), H, W2, (long long)H * 8,
                         C::RPB, C::BOXK, 8};
     int groups = (orows + C::RPB - 1) / C::RPB;
     int grid = groups < cap ? groups : cap;
+    float* nf = nullptr;
+    unsigned* np = nullptr;
     if (arg && sum)
         emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM,
-                   zf::k_row_c2r<W2, zf::kRunningStats>, map, out, arg, sum, sumsq, tw, orows, ocols,
-                   ocols, tindex, reset, &g_status);
+                   zf::k_row_c2r<W2, zf::kRunningStats>, map, out, arg, sum, sumsq, np, tw, orows,
+                   ocols, ocols, tindex, reset, &g_status);
     else if (arg)
         emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_row_c2r<W2, zf::kRunningMax>,
-                   map, out, arg, (float*)nullptr, (float*)nullptr, tw, orows, ocols, ocols, tindex,
-                   reset, &g_status);
+                   map, out, arg, nf, nf, np, tw, orows, ocols, ocols, tindex, reset, &g_status);
+    else if (peak)
+        emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_row_c2r<W2, zf::kStorePeak>,
+                   map, out, (int*)nullptr, nf, nf, peak, tw, orows, ocols, ocols, 0, 0, &g_status);
     else
         emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_row_c2r<W2, zf::kStoreMap>,
-                   map, out, (int*)nullptr, (float*)nullptr, (float*)nullptr, tw, orows, ocols, ocols,
-                   0, 0, &g_status);
+                   map, out, (int*)nullptr, nf, nf, np, tw, orows, ocols, ocols, 0, 0, &g_status);
 }
 
 #define EMU_SIZES(X) X(64) X(128) X(256) X(512) X(2048) X(120) X(240)
@@ -309,10 +342,12 @@ static void r2c(int W, int nz, const float* tm, float2* R, const float2* tw, int
     std::exit(2);
 }
 static void c2r(int W, const float2* Q, int H, float* out, int* arg, float* sum, float* sumsq,
-                const float2* tw, int orows, int ocols, int tindex, int reset, int cap) {
-#define X(N)                                                                                   \
-    if (W == N)                                                                                \
-        return run_c2r<N / 2>(Q, H, out, arg, sum, sumsq, tw, orows, ocols, tindex, reset, cap);
+                unsigned* peak, const float2* tw, int orows, int ocols, int tindex, int reset,
+                int cap) {
+#define X(N)                                                                                    \
+    if (W == N)                                                                                 \
+        return run_c2r<N / 2>(Q, H, out, arg, sum, sumsq, peak, tw, orows, ocols, tindex, reset, \
+                              cap);
     EMU_SIZES(X)
 #undef X
     std::fprintf(stderr, "unsupported W %d\n", W);
@@ -369,8 +404,9 @@ int main(int argc, char** argv) {
     const int B = hd[0], sy = hd[1], sx = hd[2], H = hd[3], W = hd[4], oy = hd[5], ox = hd[6];
     const bool conj = hd[7] != 0;
     const int cap = hd[8], nz_col = hd[9], nz_row = hd[10], chunk = hd[11];
-    const bool max_mode = hd[12] != 0;  // fold into running max / argmax maps
-    const bool stats = hd[12] == 2;     // ... and into sum / sum-of-squares maps
+    const bool max_mode = hd[12] == 1 || hd[12] == 2;  // fold into running max / argmax maps
+    const bool stats = hd[12] == 2;                    // ... and into sum / sum-of-squares maps
+    const bool peaks_mode = hd[12] == 3;               // maps plus per-template peaks
     const int W2 = W / 2;
     std::vector<float> tm((size_t)B * sy * sx);
     std::vector<float2> spec((size_t)(W2 + 1) * H);
@@ -391,6 +427,7 @@ int main(int argc, char** argv) {
     std::vector<float> sum(stats ? (size_t)oy * ox : 0), sumsq(stats ? (size_t)oy * ox : 0);
     float* sum_p = stats ? sum.data() : nullptr;
     float* sumsq_p = stats ? sumsq.data() : nullptr;
+    std::vector<unsigned> peak_keys(peaks_mode ? B : 0, 0u);
     auto twH = twiddles(H), twW = twiddles(W);
     const float scale = float(1.0 / (double(H) * double(W)));
     const int step = chunk > 0 ? chunk : 1;
@@ -411,11 +448,11 @@ int main(int argc, char** argv) {
             }
             col(H, conj, nz_col, Q, Rt, rp, spec.data(), twH.data(), sy, W2, oy, cap);
             if (max_mode)
-                c2r(W, Q, H, out.data(), arg.data(), sum_p, sumsq_p, twW.data(), oy, ox, t, t == 0,
-                    cap);
+                c2r(W, Q, H, out.data(), arg.data(), sum_p, sumsq_p, nullptr, twW.data(), oy, ox, t,
+                    t == 0, cap);
             else
                 c2r(W, Q, H, out.data() + (size_t)t * oy * ox, nullptr, nullptr, nullptr,
-                    twW.data(), oy, ox, 0, 0, cap);
+                    peaks_mode ? peak_keys.data() + t : nullptr, twW.data(), oy, ox, 0, 0, cap);
         }
     }
     if (g_status != 0) {
@@ -429,6 +466,10 @@ int main(int argc, char** argv) {
     if (stats) {
         std::fwrite(sum.data(), sizeof(float), sum.size(), g);
         std::fwrite(sumsq.data(), sizeof(float), sumsq.size(), g);
+    }
+    for (unsigned k : peak_keys) {
+        const float v = zf::key_value(k);
+        std::fwrite(&v, sizeof(float), 1, g);
     }
     std::fclose(g);
     return 0;

@@ -63,7 +63,7 @@ def run_emu(exe, tmp_path, B, sy, sx, H, W, conj, full, nz_col=None, nz_row=None
     res = subprocess.run([exe, fin, fout], capture_output=True, text=True)
     assert res.returncode == 0, res.stderr[-4000:]
     ref = O.padded_corr2d_f64(tm, spec, H, W, conj, full)
-    if max_mode:
+    if max_mode in (1, 2):  # True counts as 1
         raw = np.fromfile(fout, np.uint8)
         n = oy * ox * 4
         mx = raw[:n].view(np.float32).reshape(oy, ox)
@@ -73,7 +73,10 @@ def run_emu(exe, tmp_path, B, sy, sx, H, W, conj, full, nz_col=None, nz_row=None
             sq = raw[3 * n:4 * n].view(np.float32).reshape(oy, ox)
             return (mx, am, sm, sq), ref
         return (mx, am), ref
-    out = np.fromfile(fout, np.float32).reshape(B, oy, ox)
+    raw = np.fromfile(fout, np.float32)
+    out = raw[: B * oy * ox].reshape(B, oy, ox)
+    if max_mode == 3:
+        return (out, raw[B * oy * ox:]), ref
     return out, ref
 
 
@@ -154,3 +157,13 @@ def test_emulated_running_stats(emu, tmp_path, chunk, W, full):
     assert np.allclose(mx, ref.max(axis=0), rtol=0, atol=1e-5 * peak)
     assert O.rel_l2(ref.sum(axis=0), sm) < 1e-5
     assert O.rel_l2((ref ** 2).sum(axis=0), sq) < 1e-5
+
+
+@pytest.mark.parametrize("W,full", [(128, True), (2048, False), (240, False)])
+def test_emulated_peaks(emu, tmp_path, W, full):
+    """Maps plus each map's largest value (warp reduction and atomicMax on
+    ordered keys): the peaks equal the maxima of the stored maps exactly."""
+    B, H = 3, 64
+    (out, peaks), ref = run_emu(emu, tmp_path, B, 12, 9, H, W, True, full, max_mode=3)
+    assert O.rel_l2(ref, out) < 1e-6
+    assert np.array_equal(peaks, out.reshape(B, -1).max(axis=1))

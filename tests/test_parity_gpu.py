@@ -198,3 +198,47 @@ def test_chunked_and_in_place_layouts_agree(H, h, B):
     assert np.array_equal(a, b)
     ref = O.padded_corr2d_f64(tm[B - 1].numpy(), spec.numpy(), H, H, True, True)
     assert_parity(ref, a[B - 1], what="chunked layout, last template")
+
+
+@pytest.mark.parametrize("B,sy,sx,H,W,full", [(5, 256, 256, 4096, 4096, True),
+                                              (3, 31, 17, 512, 256, False),
+                                              (1, 100, 90, 1920, 3840, False)])
+def test_corr_peaks_equal_map_maxima(B, sy, sx, H, W, full):
+    """corr(..., peaks=): each template's largest output value, folded in by
+    the kernel that writes the map, equals the maximum of the stored map bit
+    for bit; the maps are the same as without peaks."""
+    import zipfft
+
+    _, tm, spec = make_inputs(B, sy, sx, H, W, seed=B + sy + H)
+    dev = torch.device("cuda", 0)
+    oy, ox = O.out_shape(sy, sx, H, W, full)
+    ws = torch.empty((B, H, W // 2 + 1), dtype=torch.complex64, device=dev)
+    tm_d, sp_d = tm.to(dev), spec.to(dev)
+    out = torch.full((B, oy, ox), float("nan"), device=dev)
+    peaks = torch.full((B,), float("nan"), device=dev)
+    zipfft.padded_rconv2d.corr(tm_d, ws, sp_d, out, H, W, peaks=peaks)
+    ref_out = torch.empty_like(out)
+    zipfft.padded_rconv2d.corr(tm_d, ws, sp_d, ref_out, H, W)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref_out)
+    assert torch.equal(peaks, out.reshape(B, -1).amax(dim=1))
+    if B == 1:  # 2D input, one peak
+        p1 = torch.empty(1, device=dev)
+        zipfft.padded_rconv2d.corr(tm_d[0], ws[0], sp_d, out[0], H, W, peaks=p1)
+        torch.cuda.synchronize()
+        assert torch.equal(p1, peaks)
+
+
+def test_corr_peaks_argument_errors():
+    import zipfft
+
+    _, tm, spec = make_inputs(2, 16, 16, 64, 64, seed=1)
+    dev = torch.device("cuda", 0)
+    ws = torch.empty((2, 64, 33), dtype=torch.complex64, device=dev)
+    out = torch.empty((2, 64, 64), device=dev)
+    with pytest.raises(RuntimeError, match="one per template"):
+        zipfft.padded_rconv2d.corr(tm.to(dev), ws, spec.to(dev), out, 64, 64,
+                                   peaks=torch.empty(3, device=dev))
+    with pytest.raises(RuntimeError, match="float32"):
+        zipfft.padded_rconv2d.corr(tm.to(dev), ws, spec.to(dev), out, 64, 64,
+                                   peaks=torch.empty(2, dtype=torch.float64, device=dev))

@@ -31,6 +31,9 @@ SIGNATURES = {
     "zfft_padded_real_corr_2d_max": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _c_size, _vp, _vp,
                                               _vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                                               _c_int, _vp]),
+    "zfft_padded_real_corr_2d_peaks": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _c_size, _vp,
+                                                _vp, _c_int, _c_int, _c_int, _c_int, _vp, _c_int,
+                                                _vp]),
     "zfft_padded_real_corr_2d_max_stats": (_c_int, [_vp, _c_int, _c_int, _c_int, _vp, _c_size,
                                                     _vp, _vp, _vp, _vp, _vp, _c_int, _c_int,
                                                     _c_int, _c_int, _c_int, _c_int, _c_int, _vp]),

@@ -25,6 +25,10 @@
 #include "fft_core.cuh"
 #include "launch.h"
 
+namespace zf {
+__global__ void k_peak_values(unsigned* keys, int n);
+}
+
 namespace {
 
 constexpr int kVersion = 200;  // 0.2.0
@@ -197,8 +201,8 @@ using R2cFn = cudaError_t (*)(const float*, float2*, const float2*, int, int, in
                               float, int, int, cudaStream_t);
 using ColFwdFn = cudaError_t (*)(float2*, const float2*, int, int*, int, cudaStream_t);
 using QmapFn = cudaError_t (*)(const float2*, int, CUtensorMap*);
-using C2rFn = cudaError_t (*)(const CUtensorMap*, float*, int*, float*, float*, const float2*, int,
-                              int, int, int, int, int*, int, cudaStream_t);
+using C2rFn = cudaError_t (*)(const CUtensorMap*, float*, int*, float*, float*, unsigned*,
+                              const float2*, int, int, int, int, int, int*, int, cudaStream_t);
 
 ColFn col_fn(int n) {
 #define ZF_X(N) \
@@ -274,11 +278,12 @@ const int kConfigs[][6] = {
 // maps of oy x ox.  Otherwise output / arg are the running max / argmax maps
 // (oy x ox) that every template folds into, template t with index
 // tindex_base + t; reset: the first template overwrites them.  With sum (and
-// sumsq) also given, every template is added to those maps as well.
+// sumsq) also given, every template is added to those maps as well.  With
+// peaks (maps mode only), peaks[t] receives the largest value of map t.
 int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes,
         const void* conv_data, float* output, int oy, int ox, int H, int W, bool conj,
         int device, void* stream, int* arg = nullptr, int tindex_base = 0, bool reset = false,
-        float* sum = nullptr, float* sumsq = nullptr) {
+        float* sum = nullptr, float* sumsq = nullptr, float* peaks = nullptr) {
     g_last_error.clear();
     if (batch < 0) return fail(ZFFT_ERROR_INVALID_VALUE, "batch must be >= 0. Got %d.", batch);
     if (sy < 1 || sx < 1)
@@ -316,6 +321,7 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
     if (arg && !aligned(arg, 4)) return fail(ZFFT_ERROR_INVALID_VALUE, "misaligned argmax map");
     if ((sum && !aligned(sum, 4)) || (sumsq && !aligned(sumsq, 4)))
         return fail(ZFFT_ERROR_INVALID_VALUE, "misaligned sum map");
+    if (peaks && !aligned(peaks, 4)) return fail(ZFFT_ERROR_INVALID_VALUE, "misaligned peaks");
     if (!aligned(input, 4) || !aligned(output, 4) || !aligned(ws, 16) || !aligned(conv_data, 16))
         return fail(ZFFT_ERROR_INVALID_VALUE,
                     "misaligned pointer: input/output need 4-byte alignment, fft_workspace and "
@@ -371,6 +377,11 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
     C2rFn c2r = c2r_fn(W);
 
     if (g_timer.on) g_timer.device = device;
+    unsigned* peak_keys = reinterpret_cast<unsigned*>(peaks);
+    if (peaks) {  // key 0 is below every value's key
+        e = cudaMemsetAsync(peaks, 0, sizeof(float) * (size_t)batch, s);
+        if (e != cudaSuccess) return cuda_fail(e, "clearing the peaks");
+    }
     const int step = chunk > 0 ? chunk : 1;
     for (int t0 = 0; t0 < batch; t0 += step) {
         const int n = batch - t0 < step ? batch - t0 : step;
@@ -404,15 +415,20 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
             if ((e = trace_sync(s, "k_col_fused", t)) != cudaSuccess) return cuda_fail(e, "k_col_fused");
             m = timer_mark(s);
             if (arg)
-                e = c2r(&qmap, output, arg, sum, sumsq, twW, oy, ox, ox, tindex_base + t,
+                e = c2r(&qmap, output, arg, sum, sumsq, nullptr, twW, oy, ox, ox, tindex_base + t,
                         (reset && t == 0) ? 1 : 0, status, device, s);
             else
-                e = c2r(&qmap, output + (size_t)t * oy * ox, nullptr, nullptr, nullptr, twW, oy, ox,
-                        ox, 0, 0, status, device, s);
+                e = c2r(&qmap, output + (size_t)t * oy * ox, nullptr, nullptr, nullptr,
+                        peak_keys ? peak_keys + t : nullptr, twW, oy, ox, ox, 0, 0, status, device,
+                        s);
             if (e != cudaSuccess) return cuda_fail(e, "row c2r launch");
             timer_close(2, m, s);
             if ((e = trace_sync(s, "k_row_c2r", t)) != cudaSuccess) return cuda_fail(e, "k_row_c2r");
         }
+    }
+    if (peaks) {
+        zf::k_peak_values<<<(batch + 255) / 256, 256, 0, s>>>(peak_keys, batch);
+        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(e, "peak conversion launch");
     }
     return ZFFT_SUCCESS;
 }
@@ -486,6 +502,12 @@ __device__ __forceinline__ void unpack_key(long long key, float* v, int* idx) {
     *v = __uint_as_float(u);
     *idx = int(0xFFFFFFFFu - uint32_t(k));
 }
+// Peaks: ordered keys (see ordered_key) -> float values, in place.
+__global__ void k_peak_values(unsigned* keys, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) reinterpret_cast<float*>(keys)[i] = key_value(keys[i]);
+}
+
 __global__ void k_pack_keys(const float* __restrict__ v, const int* __restrict__ idx,
                             long long* __restrict__ keys, long long n) {
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
@@ -622,6 +644,17 @@ int zfft_padded_real_corr_2d_max(const float* input, int batch, int signal_y, in
     return run(input, batch, signal_y, signal_x, fft_workspace, fft_workspace_bytes, conv_data,
                max_map, output_y, output_x, fft_size_y, fft_size_x, true, device, stream,
                reinterpret_cast<int*>(arg_map), template_index_base, reset != 0);
+}
+
+int zfft_padded_real_corr_2d_peaks(const float* input, int batch, int signal_y, int signal_x,
+                                   void* fft_workspace, size_t fft_workspace_bytes,
+                                   const void* conv_data, float* output, int output_y,
+                                   int output_x, int fft_size_y, int fft_size_x, float* peaks,
+                                   int device, void* stream) {
+    if (!peaks && batch > 0) return fail(ZFFT_ERROR_INVALID_VALUE, "null peaks");
+    return run(input, batch, signal_y, signal_x, fft_workspace, fft_workspace_bytes, conv_data,
+               output, output_y, output_x, fft_size_y, fft_size_x, true, device, stream, nullptr, 0,
+               false, nullptr, nullptr, peaks);
 }
 
 int zfft_padded_real_corr_2d_max_stats(const float* input, int batch, int signal_y,

@@ -19,6 +19,7 @@
 // the host in double precision and rounded once to float.
 #pragma once
 
+#include <cstring>
 #include <type_traits>
 
 #if defined(__CUDACC__)
@@ -33,6 +34,20 @@
 #endif
 
 namespace zf {
+
+// Order-preserving unsigned key of a float (larger float, larger key; 0 is
+// below every float's key), for atomicMax on unsigned words, and its inverse.
+ZF_HD unsigned ordered_key(float v) {
+    unsigned u;
+    memcpy(&u, &v, 4);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+ZF_HD float key_value(unsigned k) {
+    const unsigned u = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
+    float v;
+    memcpy(&v, &u, 4);
+    return v;
+}
 
 // ---------------------------------------------------------------------------
 // Compile-time trigonometry (double precision Taylor series)

@@ -116,8 +116,8 @@ cudaError_t col_fwd_t(float2* spec, const float2* tw, int W2, int* status, int d
 
 template <int W2, int MODE>
 cudaError_t c2r_t(const CUtensorMap* qmap, float* out, int* arg, float* sum, float* sumsq,
-                  const float2* tw, int out_rows, int out_cols, int out_pitch, int tindex,
-                  int reset, int* status, int device, cudaStream_t s) {
+                  unsigned* peak, const float2* tw, int out_rows, int out_cols, int out_pitch,
+                  int tindex, int reset, int* status, int device, cudaStream_t s) {
     using C = C2rCfg<W2>;
     static KernelState st;
     auto kernel = k_row_c2r<W2, MODE>;
@@ -126,8 +126,8 @@ cudaError_t c2r_t(const CUtensorMap* qmap, float* out, int* arg, float* sum, flo
     if (e != cudaSuccess) return e;
     const int groups = (out_rows + C::RPB - 1) / C::RPB;
     const int grid = min_int(groups, cap);
-    return launch_pdl(kernel, dim3(grid), C::THREADS, C::SMEM, s, *qmap, out, arg, sum, sumsq, tw,
-                      out_rows, out_cols, out_pitch, tindex, reset, status);
+    return launch_pdl(kernel, dim3(grid), C::THREADS, C::SMEM, s, *qmap, out, arg, sum, sumsq, peak,
+                      tw, out_rows, out_cols, out_pitch, tindex, reset, status);
 }
 
 // The pruned starts (nz = 1, 2) are instantiated for sizes >= 1024, where
@@ -179,18 +179,22 @@ cudaError_t ZF_CAT(make_qmap_, ZF_SIZE)(const float2* Q, int H, CUtensorMap* map
 }
 
 cudaError_t ZF_CAT(launch_row_c2r_, ZF_SIZE)(const CUtensorMap* qmap, float* out, int* arg,
-                                             float* sum, float* sumsq, const float2* tw,
-                                             int out_rows, int out_cols, int out_pitch, int tindex,
-                                             int reset, int* status, int device, cudaStream_t s) {
+                                             float* sum, float* sumsq, unsigned* peak,
+                                             const float2* tw, int out_rows, int out_cols,
+                                             int out_pitch, int tindex, int reset, int* status,
+                                             int device, cudaStream_t s) {
     constexpr int W2 = ZF_SIZE / 2;
     if (arg != nullptr && sum != nullptr)
-        return c2r_t<W2, kRunningStats>(qmap, out, arg, sum, sumsq, tw, out_rows, out_cols,
-                                        out_pitch, tindex, reset, status, device, s);
+        return c2r_t<W2, kRunningStats>(qmap, out, arg, sum, sumsq, nullptr, tw, out_rows,
+                                        out_cols, out_pitch, tindex, reset, status, device, s);
     if (arg != nullptr)
-        return c2r_t<W2, kRunningMax>(qmap, out, arg, nullptr, nullptr, tw, out_rows, out_cols,
-                                      out_pitch, tindex, reset, status, device, s);
-    return c2r_t<W2, kStoreMap>(qmap, out, nullptr, nullptr, nullptr, tw, out_rows, out_cols,
-                                out_pitch, 0, 0, status, device, s);
+        return c2r_t<W2, kRunningMax>(qmap, out, arg, nullptr, nullptr, nullptr, tw, out_rows,
+                                      out_cols, out_pitch, tindex, reset, status, device, s);
+    if (peak != nullptr)
+        return c2r_t<W2, kStorePeak>(qmap, out, nullptr, nullptr, nullptr, peak, tw, out_rows,
+                                     out_cols, out_pitch, 0, 0, status, device, s);
+    return c2r_t<W2, kStoreMap>(qmap, out, nullptr, nullptr, nullptr, nullptr, tw, out_rows,
+                                out_cols, out_pitch, 0, 0, status, device, s);
 }
 
 }  // namespace zf

@@ -22,7 +22,9 @@ namespace zf {
 // out_cols values at out_pitch.  arg == nullptr: store the map into out;
 // otherwise fold it into the running max (out) / argmax (arg) maps with
 // template index tindex (reset: overwrite instead of compare), and with sum
-// != nullptr also add it and its square to the sum / sumsq maps.
+// != nullptr also add it and its square to the sum / sumsq maps.  With
+// arg == nullptr and peak != nullptr, the map's largest value is also folded
+// into *peak as an ordered_key (atomicMax).
 #define ZF_DECL(N)                                                                              \
     cudaError_t launch_row_r2c_##N(const float* tmpl, float2* R, const float2* tw, int h, int w, \
                                    int r_pitch, long long r_tstride, int ntemplates, float scale, \
@@ -34,9 +36,9 @@ namespace zf {
                                    int device, cudaStream_t s);                                  \
     cudaError_t make_qmap_##N(const float2* Q, int H, CUtensorMap* map);                        \
     cudaError_t launch_row_c2r_##N(const CUtensorMap* qmap, float* out, int* arg, float* sum,   \
-                                   float* sumsq, const float2* tw, int out_rows, int out_cols,   \
-                                   int out_pitch, int tindex, int reset, int* status,            \
-                                   int device, cudaStream_t s);
+                                   float* sumsq, unsigned* peak, const float2* tw, int out_rows, \
+                                   int out_cols, int out_pitch, int tindex, int reset,           \
+                                   int* status, int device, cudaStream_t s);
 ZF_FOR_EACH_FFT_SIZE(ZF_DECL)
 #undef ZF_DECL
 

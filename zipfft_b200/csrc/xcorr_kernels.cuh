@@ -571,6 +571,8 @@ struct C2rCfg {
 constexpr int kStoreMap = 0;  // write the correlation map
 constexpr int kRunningMax = 1;  // fold it into a running per-pixel max / argmax
 constexpr int kRunningStats = 2;  // ... and into per-pixel sum and sum of squares
+constexpr int kStorePeak = 3;  // write the map and fold its maximum into *peak
+
 
 // MODE kStoreMap: out[y][x] = correlation.  MODE kRunningMax: out is the
 // running maximum map and arg the template-index map (same pitch); where the
@@ -584,8 +586,8 @@ template <int W2, int MODE>
 __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     k_row_c2r(const __grid_constant__ CUtensorMap qmap, float* __restrict__ out,
               int* __restrict__ arg, float* __restrict__ sum, float* __restrict__ sumsq,
-              const float2* __restrict__ twW, int out_rows, int out_cols, int out_pitch,
-              int tindex, int reset, int* __restrict__ status) {
+              unsigned* __restrict__ peak, const float2* __restrict__ twW, int out_rows,
+              int out_cols, int out_pitch, int tindex, int reset, int* __restrict__ status) {
     using C = C2rCfg<W2>;
     using I = Stockham<W2, C::T, true, false>;
     static_assert(I::S >= 2, "row FFT needs at least two stages");
@@ -696,9 +698,10 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
         I::run_regs(v, xbuf, tw, t);
 
         const int y = grp * C::RPB + g;
+        float pk = -INFINITY;  // kStorePeak: this thread's largest stored value
         if (y < out_rows) {
             float* orow = out + (size_t)y * out_pitch;
-            if constexpr (MODE == kStoreMap) {
+            if constexpr (MODE == kStoreMap || MODE == kStorePeak) {
 #pragma unroll
                 for (int q = 0; q < I::bpt(I::S - 1); ++q) {
                     const int bb = t + q * C::T;
@@ -709,9 +712,16 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                             const float2 z = v[q * RL + r];
                             if (vec_ok) {
                                 st_hint(reinterpret_cast<float2*>(orow) + m, z, pol_stream);
+                                if constexpr (MODE == kStorePeak) pk = fmaxf(pk, fmaxf(z.x, z.y));
                             } else {
-                                if (2 * m < out_cols) st_hint(orow + 2 * m, z.x, pol_stream);
-                                if (2 * m + 1 < out_cols) st_hint(orow + 2 * m + 1, z.y, pol_stream);
+                                if (2 * m < out_cols) {
+                                    st_hint(orow + 2 * m, z.x, pol_stream);
+                                    if constexpr (MODE == kStorePeak) pk = fmaxf(pk, z.x);
+                                }
+                                if (2 * m + 1 < out_cols) {
+                                    st_hint(orow + 2 * m + 1, z.y, pol_stream);
+                                    if constexpr (MODE == kStorePeak) pk = fmaxf(pk, z.y);
+                                }
                             }
                         }
                     }
@@ -826,6 +836,13 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                     }
                 }
             }
+        }
+        if constexpr (MODE == kStorePeak) {
+            // Every lane takes part (rows past the end contribute -inf); one
+            // atomic per warp.
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) pk = fmaxf(pk, __shfl_xor_sync(0xffffffffu, pk, o));
+            if ((tid & 31) == 0) atomicMax(peak, ordered_key(pk));
         }
     }
 }

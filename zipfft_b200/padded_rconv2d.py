@@ -116,14 +116,37 @@ def _run(fn_name: str, input, fft_workspace, conv_data, output, fft_size_y: int,
 
 
 def corr(input: torch.Tensor, fft_workspace: torch.Tensor, conv_data: torch.Tensor,
-         output: torch.Tensor, fft_size_y: int, fft_size_x: int) -> None:
+         output: torch.Tensor, fft_size_y: int, fft_size_x: int, *,
+         peaks: torch.Tensor = None) -> None:
     """2D padded real cross-correlation (binding.cu:295-299, :304).
 
     input (h, w) or (B, h, w) float32; fft_workspace complex64 (H, W/2+1) or
     (B, H, W/2+1), clobbered; conv_data complex64 (W/2+1, H) = rfftn(image).T;
-    output float32 (..., H-h+1, W-w+1) or (..., H, W), written in place."""
-    _run("zfft_padded_real_corr_2d", input, fft_workspace, conv_data, output, fft_size_y,
-         fft_size_x)
+    output float32 (..., H-h+1, W-w+1) or (..., H, W), written in place.
+
+    peaks (keyword only, not in the reference): a float32 tensor of B values
+    (one per template; 1 value for a 2D input) that receives each output
+    map's largest value, computed by the kernel that writes the map."""
+    if peaks is None:
+        _run("zfft_padded_real_corr_2d", input, fft_workspace, conv_data, output, fft_size_y,
+             fft_size_x)
+        return
+    batch, sy, sx, oy, ox = _validate(input, fft_workspace, conv_data, output, int(fft_size_y),
+                                      int(fft_size_x))
+    _check(peaks.dtype == torch.float32, "Peaks tensor must be of type torch.float32")
+    _check(peaks.device == input.device, "Peaks tensor must be on the same device as the input")
+    _check(peaks.numel() == batch and peaks.is_contiguous(),
+           f"Peaks tensor must be contiguous with {batch} elements (one per template)")
+    lib = _lib.load()
+    device = input.device.index if input.device.index is not None else torch.cuda.current_device()
+    stream = torch.cuda.current_stream(device).cuda_stream
+    ws_bytes = fft_workspace.numel() * fft_workspace.element_size()
+    status = lib.zfft_padded_real_corr_2d_peaks(input.data_ptr(), batch, sy, sx,
+                                                fft_workspace.data_ptr(), ws_bytes,
+                                                conv_data.data_ptr(), output.data_ptr(), oy, ox,
+                                                int(fft_size_y), int(fft_size_x),
+                                                peaks.data_ptr(), device, stream)
+    _lib.check(status)
 
 
 def conv(input: torch.Tensor, fft_workspace: torch.Tensor, conv_data: torch.Tensor,
