@@ -269,10 +269,10 @@ template <int W2, int NZ>
 void run_r2c(const float* tm, float2* R, const float2* tw, int h, int w, int r_pitch,
              long long r_tstride, int nt, float sc, int cap) {
     using C = zf::R2cCfg<W2>;
-    int groups = (h + C::RPB - 1) / C::RPB;
-    int per = groups < cap ? groups : cap;
-    emu_launch(dim3{(unsigned)per, (unsigned)nt, 1}, C::THREADS, C::SMEM, zf::k_row_r2c<W2, NZ>, tm,
-               R, tw, h, w, r_pitch, r_tstride, sc);
+    int units = ((h + 1) / 2 * 2 + C::RPB - 1) / C::RPB * nt;
+    int grid = units < cap ? units : cap;
+    emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_row_r2c<W2, NZ>, tm, R, tw, h,
+               w, r_pitch, r_tstride, nt, sc);
 }
 template <int H>
 void run_col_fwd(float2* spec, const float2* tw, int W2, int cap) {

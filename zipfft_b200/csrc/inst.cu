@@ -78,12 +78,11 @@ cudaError_t r2c_t(const float* tmpl, float2* R, const float2* tw, int h, int w, 
     int cap = 0;
     cudaError_t e = configure(kernel, st, C::SMEM, C::THREADS, device, &cap);
     if (e != cudaSuccess) return e;
-    // Blocks per template: enough to fill the GPU over the whole chunk.
-    const int groups = (h + C::RPB - 1) / C::RPB;
-    const int per_t = min_int(groups, (cap + ntemplates - 1) / ntemplates);
-    dim3 grid(per_t > 0 ? per_t : 1, ntemplates);
-    return launch_pdl(kernel, grid, C::THREADS, C::SMEM, s, tmpl, R, tw, h, w, r_pitch, r_tstride,
-                      scale);
+    // One wave of co-resident blocks over all (template, row group) pairs.
+    const long long units = (long long)((h + 1) / 2 * 2 + C::RPB - 1) / C::RPB * ntemplates;
+    const int grid = (int)(units < cap ? units : cap);
+    return launch_pdl(kernel, dim3(grid > 0 ? grid : 1), C::THREADS, C::SMEM, s, tmpl, R, tw, h, w,
+                      r_pitch, r_tstride, ntemplates, scale);
 }
 
 template <int H, bool CONJ, int NZ>

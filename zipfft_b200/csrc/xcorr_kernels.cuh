@@ -66,7 +66,8 @@ constexpr bool plan_palindrome(int n) {
 // ===========================================================================
 // Kernel 1: forward real FFT of template rows (W2-point complex FFT of
 // z[m] = x[2m] + i x[2m+1] plus the split post-pass), packed and scaled.
-// grid.y indexes templates; blocks loop over row groups of one template.
+// The (template, row group) pairs of all ntemplates templates form one index
+// space that a single wave of blocks strides through.
 // ===========================================================================
 template <int W2>
 struct R2cCfg {
@@ -92,7 +93,7 @@ struct RowLoader {
 template <int W2, int NZ>
 __global__ void __launch_bounds__(R2cCfg<W2>::THREADS)
     k_row_r2c(const float* __restrict__ tmpl, float2* __restrict__ R, const float2* __restrict__ twW,
-              int h, int w, int r_pitch, long long r_tstride, float scale) {
+              int h, int w, int r_pitch, long long r_tstride, int ntemplates, float scale) {
     using C = R2cCfg<W2>;
     using F = Stockham<W2, C::T, false, false>;
     static_assert(F::S >= 2, "row FFT needs at least two stages");
@@ -102,8 +103,6 @@ __global__ void __launch_bounds__(R2cCfg<W2>::THREADS)
     const int g = tid / C::T, t = tid % C::T;
     float2* smem = dyn_smem();
     float2* buf = smem + g * C::XB;
-    const float* tm = tmpl + (size_t)blockIdx.y * h * w;
-    float2* Rt = R + (size_t)blockIdx.y * r_tstride;
 
     pdl_launch_dependents();
     typename F::Twiddles tw;
@@ -114,7 +113,12 @@ __global__ void __launch_bounds__(R2cCfg<W2>::THREADS)
     // Row groups cover rows [0, round_up(h, 2)): the padding row of an odd h
     // is written as zeros by the split pass below.
     const int h_pad = (h + 1) & ~1;
-    for (int n0 = blockIdx.x * C::RPB; n0 < h_pad; n0 += gridDim.x * C::RPB) {
+    const int groups = (h_pad + C::RPB - 1) / C::RPB;
+    const int units = groups * ntemplates;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+        const int tj = u / groups, n0 = (u - tj * groups) * C::RPB;
+        const float* tm = tmpl + (size_t)tj * h * w;
+        float2* Rt = R + (size_t)tj * r_tstride;
         const int n = n0 + g;
         RowLoader ld{tm + (size_t)(n < h ? n : 0) * w, n < h ? w : 0};
         float2 v[F::MAXE];
