@@ -33,7 +33,9 @@
 #include <thread>
 #include <vector>
 
-struct float2 {
+// 8-byte aligned like CUDA's float2, so that the alignment sanitizer flags
+// an 8-byte access at a 4-byte aligned address.
+struct __attribute__((aligned(8))) float2 {
     float x, y;
 };
 struct __attribute__((aligned(8))) int2 {

@@ -29,8 +29,9 @@ def emu():
         pytest.skip("g++ not available")
     if not os.path.exists(EXE) or os.path.getmtime(EXE) < _deps():
         os.makedirs(os.path.dirname(EXE), exist_ok=True)
-        subprocess.check_call(["g++", "-std=c++20", "-O1", "-g", "-fsanitize=address",
-                               "-fno-omit-frame-pointer", "-pthread", SRC, "-o", EXE])
+        subprocess.check_call(["g++", "-std=c++20", "-O1", "-g", "-fsanitize=address,alignment",
+                               "-fno-sanitize-recover=alignment", "-fno-omit-frame-pointer",
+                               "-pthread", SRC, "-o", EXE])
     return EXE
 
 
@@ -112,19 +113,21 @@ def test_emulated_kernels_match_oracle(emu, tmp_path, case):
     assert O.max_abs_over_peak(ref, out) < 1e-5
 
 
-@pytest.mark.parametrize("chunk,W", [(0, 128), (2, 128), (0, 2048)])
-def test_emulated_running_max_argmax(emu, tmp_path, chunk, W):
-    """The max / argmax epilogue of the inverse row pass."""
+@pytest.mark.parametrize("chunk,W,sx", [(0, 128, 9), (2, 128, 9), (0, 2048, 9), (0, 256, 10)])
+def test_emulated_running_max_argmax(emu, tmp_path, chunk, W, sx):
+    """The max / argmax epilogue of the inverse row pass (sx = 10: odd-width
+    valid crop, 8-byte accesses on every other row only)."""
     B, H = 5, 64
-    (mx, am), ref = run_emu(emu, tmp_path, B, 12, 9, H, W, True, True, chunk=chunk, max_mode=True)
+    (mx, am), ref = run_emu(emu, tmp_path, B, 12, sx, H, W, True, True, chunk=chunk,
+                            max_mode=True)
     assert np.allclose(mx, ref.max(axis=0), rtol=0, atol=1e-5 * np.abs(ref).max())
     order = np.sort(ref, axis=0)
     margin = order[-1] - order[-2]
     sure = margin > 1e-4 * np.abs(ref).max()
     assert sure.mean() > 0.99
     assert np.array_equal(am[sure], ref.argmax(axis=0)[sure])
-    (mv, av), refv = run_emu(emu, tmp_path, B, 12, 9, H, W, True, False, max_mode=True)
-    assert mv.shape == (H - 11, W - 8)
+    (mv, av), refv = run_emu(emu, tmp_path, B, 12, sx, H, W, True, False, max_mode=True)
+    assert mv.shape == (H - 11, W - sx + 1)
     assert np.allclose(mv, refv.max(axis=0), rtol=0, atol=1e-5 * np.abs(refv).max())
 
 
@@ -147,11 +150,12 @@ def test_emulated_image_spectrum(emu, tmp_path, H, W):
     assert np.abs(out - ref).max() < 1e-5 * np.abs(ref).max()
 
 
-@pytest.mark.parametrize("chunk,W,full", [(0, 128, True), (2, 2048, False)])
-def test_emulated_running_stats(emu, tmp_path, chunk, W, full):
+@pytest.mark.parametrize("chunk,W,full,sx", [(0, 128, True, 9), (2, 2048, False, 9),
+                                             (0, 256, False, 10)])
+def test_emulated_running_stats(emu, tmp_path, chunk, W, full, sx):
     """The max / argmax epilogue with per-pixel sum and sum of squares."""
     B, H = 5, 64
-    (mx, am, sm, sq), ref = run_emu(emu, tmp_path, B, 12, 9, H, W, True, full, chunk=chunk,
+    (mx, am, sm, sq), ref = run_emu(emu, tmp_path, B, 12, sx, H, W, True, full, chunk=chunk,
                                     max_mode=2)
     peak = np.abs(ref).max()
     assert np.allclose(mx, ref.max(axis=0), rtol=0, atol=1e-5 * peak)
@@ -159,11 +163,12 @@ def test_emulated_running_stats(emu, tmp_path, chunk, W, full):
     assert O.rel_l2((ref ** 2).sum(axis=0), sq) < 1e-5
 
 
-@pytest.mark.parametrize("W,full", [(128, True), (2048, False), (240, False)])
-def test_emulated_peaks(emu, tmp_path, W, full):
+@pytest.mark.parametrize("W,full,sx", [(128, True, 9), (2048, False, 9), (240, False, 9),
+                                       (2048, False, 10)])
+def test_emulated_peaks(emu, tmp_path, W, full, sx):
     """Maps plus each map's largest value (warp reduction and atomicMax on
     ordered keys): the peaks equal the maxima of the stored maps exactly."""
     B, H = 3, 64
-    (out, peaks), ref = run_emu(emu, tmp_path, B, 12, 9, H, W, True, full, max_mode=3)
+    (out, peaks), ref = run_emu(emu, tmp_path, B, 12, sx, H, W, True, full, max_mode=3)
     assert O.rel_l2(ref, out) < 1e-6
     assert np.array_equal(peaks, out.reshape(B, -1).max(axis=1))

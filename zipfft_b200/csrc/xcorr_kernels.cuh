@@ -627,8 +627,6 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     // Q comes from the previous kernel.
     pdl_wait_prerequisites();
 
-    const bool vec_ok = out_cols == 2 * W2 && (out_pitch % 2) == 0 &&
-                        (reinterpret_cast<size_t>(out) % 8) == 0;
     const int ngroups = (out_rows + C::RPB - 1) / C::RPB;
 
     // L2 policy: Q lines stay resident (the next template's column pass
@@ -705,33 +703,48 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
         float pk = -INFINITY;  // kStorePeak: this thread's largest stored value
         if (y < out_rows) {
             float* orow = out + (size_t)y * out_pitch;
+            // Element m holds outputs 2m, 2m+1: one 8-byte access where the
+            // row is 8-byte aligned and both lie inside the crop.  With an odd
+            // pitch every other row qualifies.
+            auto aligned8 = [](const void* p) { return (reinterpret_cast<size_t>(p) & 7) == 0; };
             if constexpr (MODE == kStoreMap || MODE == kStorePeak) {
+                const bool rv = aligned8(orow);
+                // Full aligned rows (the common case) take a branch-free copy
+                // of the loop; cropped or misaligned rows test each pair.
+                auto emit = [&](auto full_row) {
+                    constexpr bool FULL = decltype(full_row)::value;
 #pragma unroll
-                for (int q = 0; q < I::bpt(I::S - 1); ++q) {
-                    const int bb = t + q * C::T;
-                    if (I::even(I::S - 1) || bb < NBL) {
+                    for (int q = 0; q < I::bpt(I::S - 1); ++q) {
+                        const int bb = t + q * C::T;
+                        if (I::even(I::S - 1) || bb < NBL) {
 #pragma unroll
-                        for (int r = 0; r < RL; ++r) {
-                            const int m = bb + r * NBL;
-                            const float2 z = v[q * RL + r];
-                            if (vec_ok) {
-                                st_hint(reinterpret_cast<float2*>(orow) + m, z, pol_stream);
-                                if constexpr (MODE == kStorePeak) pk = fmaxf(pk, fmaxf(z.x, z.y));
-                            } else {
-                                if (2 * m < out_cols) {
-                                    st_hint(orow + 2 * m, z.x, pol_stream);
-                                    if constexpr (MODE == kStorePeak) pk = fmaxf(pk, z.x);
-                                }
-                                if (2 * m + 1 < out_cols) {
-                                    st_hint(orow + 2 * m + 1, z.y, pol_stream);
-                                    if constexpr (MODE == kStorePeak) pk = fmaxf(pk, z.y);
+                            for (int r = 0; r < RL; ++r) {
+                                const int m = bb + r * NBL;
+                                const float2 z = v[q * RL + r];
+                                if (FULL || (rv && 2 * m + 1 < out_cols)) {
+                                    st_hint(reinterpret_cast<float2*>(orow) + m, z, pol_stream);
+                                    if constexpr (MODE == kStorePeak) pk = fmaxf(pk, fmaxf(z.x, z.y));
+                                } else {
+                                    if (2 * m < out_cols) {
+                                        st_hint(orow + 2 * m, z.x, pol_stream);
+                                        if constexpr (MODE == kStorePeak) pk = fmaxf(pk, z.x);
+                                    }
+                                    if (2 * m + 1 < out_cols) {
+                                        st_hint(orow + 2 * m + 1, z.y, pol_stream);
+                                        if constexpr (MODE == kStorePeak) pk = fmaxf(pk, z.y);
+                                    }
                                 }
                             }
                         }
                     }
-                }
+                };
+                if (rv && out_cols == 2 * W2)
+                    emit(std::true_type{});
+                else
+                    emit(std::false_type{});
             } else {
                 int* arow = arg + (size_t)y * out_pitch;
+                const bool rv = aligned8(orow) && aligned8(arow);
                 // All loads of the stored maxima first, then the updates.
                 float2 cur[I::bpt(I::S - 1) * RL];
 #pragma unroll
@@ -742,7 +755,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                         const int m = bb + r * NBL;
                         float2 c = c_make(-INFINITY, -INFINITY);
                         if (!reset && (I::even(I::S - 1) || bb < NBL)) {
-                            if (vec_ok) {
+                            if (rv && 2 * m + 1 < out_cols) {
                                 c = reinterpret_cast<const float2*>(orow)[m];
                             } else {
                                 if (2 * m < out_cols) c.x = orow[2 * m];
@@ -762,7 +775,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                             const float2 z = v[q * RL + r];
                             const float2 c = cur[q * RL + r];
                             const bool u0 = reset || z.x > c.x, u1 = reset || z.y > c.y;
-                            if (vec_ok) {
+                            if (rv && 2 * m + 1 < out_cols) {
                                 if (u0 && u1) {
                                     reinterpret_cast<float2*>(orow)[m] = z;
                                     reinterpret_cast<int2*>(arow)[m] = make_int2(tindex, tindex);
@@ -791,6 +804,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                     // a butterfly's RL values at a time: loads first, then stores.
                     float* srow = sum + (size_t)y * out_pitch;
                     float* qrow = sumsq + (size_t)y * out_pitch;
+                    const bool rvs = aligned8(srow) && aligned8(qrow);
 #pragma unroll
                     for (int q = 0; q < I::bpt(I::S - 1); ++q) {
                         const int bb = t + q * C::T;
@@ -801,7 +815,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                                 const int m = bb + r * NBL;
                                 s1[r] = s2[r] = c_make(0.f, 0.f);
                                 if (!reset) {
-                                    if (vec_ok) {
+                                    if (rvs && 2 * m + 1 < out_cols) {
                                         s1[r] = reinterpret_cast<const float2*>(srow)[m];
                                         s2[r] = reinterpret_cast<const float2*>(qrow)[m];
                                     } else {
@@ -822,7 +836,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                                 const float2 z = v[q * RL + r];
                                 const float2 a = c_make(s1[r].x + z.x, s1[r].y + z.y);
                                 const float2 b2 = c_make(fmaf(z.x, z.x, s2[r].x), fmaf(z.y, z.y, s2[r].y));
-                                if (vec_ok) {
+                                if (rvs && 2 * m + 1 < out_cols) {
                                     reinterpret_cast<float2*>(srow)[m] = a;
                                     reinterpret_cast<float2*>(qrow)[m] = b2;
                                 } else {
