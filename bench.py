@@ -456,8 +456,9 @@ def run_search_arm(args, world, rank, local):
     torch.cuda.set_device(dev)
     image = make_image(0).to(dev)
     spec = P.image_spectrum(image)
-    g = torch.Generator().manual_seed(7)
-    tm = torch.randn((SEARCH_PER_STEP * world, SEARCH_TH, SEARCH_TH), generator=g)
+    # Each rank holds only its own shard of the template set.
+    g = torch.Generator().manual_seed(7 + rank)
+    tm = torch.randn((SEARCH_PER_STEP, SEARCH_TH, SEARCH_TH), generator=g)
     tm = ((tm - tm.mean(dim=(1, 2), keepdim=True)) / tm.std(dim=(1, 2), keepdim=True))
     tm = tm.contiguous().pin_memory()
     group = None
@@ -468,7 +469,7 @@ def run_search_arm(args, world, rank, local):
 
     def step():
         return template_search(tm, spec, H, W, batch_size=SEARCH_BATCH, full=True, group=group,
-                               stats=args.stats)
+                               stats=args.stats, shard_base=rank * SEARCH_PER_STEP)
 
     for _ in range(args.warmup):
         out = step()

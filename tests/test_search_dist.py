@@ -122,3 +122,45 @@ def test_rank_failure_ends_the_other_rank_with_an_error(tmp_path):
     assert procs[1].exitcode != 0
     assert procs[0].exitcode != 0
     assert not (tmp_path / "max0.npy").exists()
+
+
+def _shard_worker(rank, world, port, out_dir):
+    sys.path.insert(0, ROOT)
+    import datetime
+
+    import torch.distributed as dist
+
+    from tests.search_cpu_ops import CPU_OPS
+    from zipfft_b200.search import shard_range, template_search
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=10))
+    try:
+        tm, spec = _inputs(n=7)
+        lo, hi = (0, 4) if rank == 0 else (4, 7)  # uneven shards, each rank holds only its own
+        mx, am = template_search(tm[lo:hi].clone(), spec, 32, 32, batch_size=2, full=True,
+                                 device=torch.device("cpu"), ops=CPU_OPS, shard_base=lo)
+        np.save(os.path.join(out_dir, f"max{rank}.npy"), mx.numpy())
+        np.save(os.path.join(out_dir, f"arg{rank}.npy"), am.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_search_with_local_shards(tmp_path):
+    """Each rank passes only its own templates (shard_base = their first
+    global index); the combined maps equal the single-process search."""
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_shard_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    from oracle import xcorr_oracle as O
+
+    tm, spec = _inputs(n=7)
+    res = O.padded_corr2d_f64(tm.numpy(), spec.numpy(), 32, 32, True, True).astype(np.float32)
+    for r in range(2):
+        assert np.array_equal(np.load(tmp_path / f"max{r}.npy"), res.max(axis=0))
+        assert np.array_equal(np.load(tmp_path / f"arg{r}.npy"), res.argmax(axis=0))

@@ -130,8 +130,8 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
                     group=None, device: Optional[torch.device] = None,
                     ops: SearchOps = CUDA_OPS, checkpoint_every: int = 0,
                     on_checkpoint: Optional[Callable[[SearchCheckpoint], None]] = None,
-                    resume: Optional[SearchCheckpoint] = None, stats: bool = False
-                    ) -> Tuple[torch.Tensor, ...]:
+                    resume: Optional[SearchCheckpoint] = None, stats: bool = False,
+                    shard_base: Optional[int] = None) -> Tuple[torch.Tensor, ...]:
     """Maximum and argmax (global template index) of the correlation per pixel.
 
     templates: (N, h, w) float32 -- the whole set (every rank passes the same
@@ -149,7 +149,11 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
 
     stats=True: also the per-pixel sum and sum of squares of the correlations
     over all templates (float32; summed across ranks with one all-reduce), for
-    z-score normalisation; returns (max_map, arg_map, sum_map, sumsq_map)."""
+    z-score normalisation; returns (max_map, arg_map, sum_map, sumsq_map).
+
+    shard_base: `templates` is then only this rank's shard (each rank loads
+    its own templates), its first template having global index shard_base;
+    nothing is split further.  The ranks' shards must not overlap."""
     import torch.distributed as dist
 
     distributed = dist.is_available() and dist.is_initialized()
@@ -159,7 +163,13 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
     N, h, w = templates.shape
     H, W = int(fft_size_y), int(fft_size_x)
     oy, ox = (H, W) if full else (H - h + 1, W - w + 1)
-    lo, hi = shard_range(N, rank, world)
+    if shard_base is None:
+        lo, hi = shard_range(N, rank, world)
+        off = 0
+    else:
+        if shard_base < 0:
+            raise ValueError(f"shard_base must be >= 0, got {shard_base}")
+        lo, hi, off = shard_base, shard_base + N, shard_base
 
     start = lo
     if resume is not None:
@@ -202,17 +212,17 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
 
     def stage(i: int, b0: int, b1: int) -> torch.Tensor:
         if not on_host:
-            return templates[b0:b1]
+            return templates[b0 - off:b1 - off]
         buf = bufs[i][: b1 - b0]
         if copy is not None:
             copy.wait_stream(compute) if events[i] is None else copy.wait_event(events[i])
             with torch.cuda.stream(copy):
-                buf.copy_(templates[b0:b1], non_blocking=True)
+                buf.copy_(templates[b0 - off:b1 - off], non_blocking=True)
             ev = torch.cuda.Event()
             ev.record(copy)
             compute.wait_event(ev)
         else:
-            buf.copy_(templates[b0:b1])
+            buf.copy_(templates[b0 - off:b1 - off])
         return buf
 
     # A resumed shard has maps to fold into; a fresh one starts by overwriting.
