@@ -8,6 +8,14 @@
 //   k_col_fused columns kx:  Q[., kx] = IFFT_H( conj(FFT_H(pad_h(R[kx]))) . S[kx] )
 //                                                                   (cuh:58-117)
 //   k_row_c2r   rows y:      out[y] = irfft_W(Q[y, .]), cropped       (cuh:34-56)
+//               epilogues: store the map (optionally folding its maximum into a
+//               per-template peak), or fold it into running per-pixel max /
+//               argmax (optionally sum / sum of squares) maps
+//
+// and, for the image spectrum the operator takes (conv_data), k_row_r2c over
+// the image rows followed by
+//
+//   k_col_fwd   columns kx:  S[kx] = FFT_H(R[kx]), in place in conv_data
 //
 // Intermediate layout (complex64): Q is column-major, element (kx, y) at
 // kx * H + y, packed kx in [0, W2), so one H x W2 slice holds a template's
