@@ -46,7 +46,7 @@ extern "C" {
  *                 zfft_workspace_bytes(fft_y, fft_x) bytes (one
  *                 (fft_y, fft_x/2 + 1) slice, as in the reference, is always
  *                 enough; the reference's (batch, fft_y, fft_x/2 + 1) lets the
- *                 row transforms of up to 16 templates run per launch).
+ *                 row transforms of up to 32 templates run per launch).
  *                 Clobbered.
  *   conv_data     complex64 [fft_x/2 + 1][fft_y], 16-byte aligned: rfft2 of the
  *                 image, transposed (the reference's pre-transposed layout,

@@ -71,6 +71,11 @@ ZF_DEV uint64_t l2_evict_first() {
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
     return p;
 }
+ZF_DEV uint64_t l2_evict_normal() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
 ZF_DEV uint64_t l2_evict_last() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
@@ -178,6 +183,7 @@ inline bool mbar_try_wait(uint64_t* bar, uint32_t parity) { return emu_mbar_try_
 void emu_check_copy(const void* dst, const void* src, uint32_t bytes);
 inline uint64_t l2_evict_first() { return 1; }
 inline uint64_t l2_evict_last() { return 2; }
+inline uint64_t l2_evict_normal() { return 3; }
 inline void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t = 0) {
     emu_check_copy(dst, src, bytes);
     std::memcpy(dst, src, bytes);

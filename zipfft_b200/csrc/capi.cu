@@ -33,7 +33,7 @@ namespace {
 
 constexpr int kVersion = 200;  // 0.2.0
 constexpr int kMaxDevices = 64;
-constexpr int kMaxChunk = 16;  // templates per row-r2c launch
+constexpr int kMaxChunk = 32;  // templates per row-r2c launch
 
 thread_local std::string g_last_error;
 

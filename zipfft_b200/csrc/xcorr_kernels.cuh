@@ -245,10 +245,13 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
 
     const uint32_t r_bytes = (uint32_t)round_up(h, 2) * 8u;
     const int stride = gridDim.x * C::FPB;
-    // L2 policy: the spectrum and template columns stream through (each is
-    // read once per template); the intermediate Q is kept resident for the
-    // row kernel that reads it next.
+    // L2 policy: template columns stream through (read once); the spectrum,
+    // read once per template but by every template, keeps the normal policy
+    // (some of it then survives in L2 for the next template: measured faster
+    // than evict-first or evict-last); the intermediate Q is kept resident
+    // for the row kernel that reads it next.
     const uint64_t pol_stream = l2_evict_first();
+    const uint64_t pol_spec = l2_evict_normal();
     const uint64_t pol_keep = l2_evict_last();
 
     // Thread 0 fetches the spectrum and template columns of group vc0 into buffer b.
@@ -261,7 +264,7 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
             const int vc = vc0 + j;
             if (vc > W2) break;
             tma_load_1d(sbase + (b * C::FPB + j) * C::SB, spec + (size_t)vc * H, H * 8u, &mbar[b],
-                        pol_stream);
+                        pol_spec);
             const int rc = vc == W2 ? 0 : vc;
             tma_load_1d(rbase + (b * C::FPB + j) * C::RB, R + (size_t)rc * r_pitch, r_bytes,
                         &mbar[b], pol_stream);

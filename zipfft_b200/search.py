@@ -42,10 +42,10 @@ class SearchOps:
     workspace: Callable  # (H, W, h, device) -> workspace tensor
 
 
-def search_workspace_elems(H: int, W: int, h: int, chunk: int = 16) -> int:
+def search_workspace_elems(H: int, W: int, h: int, chunk: int = 32) -> int:
     """complex64 elements of a workspace holding the intermediate plus the row
-    spectra of `chunk` templates (the library then transforms the rows of 16
-    templates per launch)."""
+    spectra of `chunk` templates (the library then transforms the rows of up
+    to 32 templates per launch)."""
     h_pad = (h + 1) // 2 * 2
     return _lib.load().zfft_workspace_bytes(H, W) // 8 + chunk * (W // 2) * h_pad
 
