@@ -172,3 +172,30 @@ def test_emulated_peaks(emu, tmp_path, W, full, sx):
     (out, peaks), ref = run_emu(emu, tmp_path, B, 12, sx, H, W, True, full, max_mode=3)
     assert O.rel_l2(ref, out) < 1e-6
     assert np.array_equal(peaks, out.reshape(B, -1).max(axis=1))
+
+
+def _random_emu_cases(n, seed):
+    sizes = [64, 128, 256, 512, 120, 240]
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(n):
+        H, W = (int(x) for x in rng.choice(sizes, 2))
+        sy, sx = int(rng.integers(1, H // 2 + 1)), int(rng.integers(1, W // 2 + 1))
+        B = int(rng.integers(1, 4))
+        out.append((B, sy, sx, H, W, bool(rng.random() < 0.7), bool(rng.random() < 0.5),
+                    int(rng.choice([0, 2]))))
+    return out
+
+
+RANDOM_EMU = _random_emu_cases(8, 7)
+
+
+@pytest.mark.parametrize("case", RANDOM_EMU, ids=[str(c) for c in RANDOM_EMU])
+def test_emulated_random_shapes(emu, tmp_path, case):
+    """Seeded random shapes (sizes, template extents, corr / conv, crop,
+    chunked row passes) against the oracle."""
+    B, sy, sx, H, W, conj, full, chunk = case
+    out, ref = run_emu(emu, tmp_path, B, sy, sx, H, W, conj, full, chunk=chunk,
+                       seed=B + sy + sx)
+    assert O.rel_l2(ref, out) < 1e-6
+    assert O.max_abs_over_peak(ref, out) < 1e-5

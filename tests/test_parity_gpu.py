@@ -242,3 +242,33 @@ def test_corr_peaks_argument_errors():
     with pytest.raises(RuntimeError, match="float32"):
         zipfft.padded_rconv2d.corr(tm.to(dev), ws, spec.to(dev), out, 64, 64,
                                    peaks=torch.empty(2, dtype=torch.float64, device=dev))
+
+
+def _random_cases(n, seed):
+    """Seeded random configurations over every compiled FFT size."""
+    sizes = [64, 128, 256, 512, 1024, 2048, 4096, 120, 240, 480, 960, 1920, 3840]
+    rng = np.random.default_rng(seed)
+    cases = []
+    for _ in range(n):
+        H, W = (int(x) for x in rng.choice(sizes, 2))
+        if H * W > 4096 * 2048:  # keep the float64 oracle quick
+            W = 1024
+        sy = int(rng.integers(1, H + 1))
+        sx = int(rng.integers(1, W + 1))
+        if rng.random() < 0.6:  # mostly small templates, as in template matching
+            sy, sx = max(1, sy // 8), max(1, sx // 8)
+        B = int(rng.integers(1, 5))
+        cases.append((B, sy, sx, H, W, bool(rng.random() < 0.7), bool(rng.random() < 0.5)))
+    return cases
+
+
+RANDOM = _random_cases(24, 2026)
+
+
+@pytest.mark.parametrize("case", RANDOM, ids=[str(c) for c in RANDOM])
+def test_random_shapes_match_oracle(case):
+    B, sy, sx, H, W, conj, full = case
+    _, tm, spec = make_inputs(B, sy, sx, H, W, seed=sy * 7 + sx)
+    out = capi_corr(tm, spec, H, W, full, conj)
+    ref = O.padded_corr2d_f64(tm.numpy(), spec.numpy(), H, W, conj, full)
+    assert_parity(ref, out, what=str(case))

@@ -13,7 +13,7 @@ from typing import List
 from . import _lib
 from . import padded_rconv2d
 
-__version__ = "0.1.0"
+__version__ = "0.3.0"
 
 CUDA_ARCHITECTURES = ["10.0a"]
 

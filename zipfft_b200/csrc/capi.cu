@@ -31,7 +31,7 @@ __global__ void k_peak_values(unsigned* keys, int n);
 
 namespace {
 
-constexpr int kVersion = 200;  // 0.2.0
+constexpr int kVersion = 300;  // 0.3.0
 constexpr int kMaxDevices = 64;
 constexpr int kMaxChunk = 32;  // templates per row-r2c launch
 
