@@ -9,7 +9,7 @@
 //
 // Usage: zf_emu <in.bin> <out.bin>, or zf_emu spectrum <in.bin> <out.bin>
 //   in.bin : int32 header {B, sy, sx, H, W, oy, ox, conj, grid_cap, nz_col,
-//            nz_row, chunk, max_mode}, float32 templates [B][sy][sx],
+//            nz_row, chunk, max_mode, group}, float32 templates [B][sy][sx],
 //            complex64 spectrum [W/2+1][H]
 //   out.bin: float32 [B][oy][ox] maps, or with max_mode the float32 [oy][ox]
 //            running maximum and int32 [oy][ox] argmax over the templates,
@@ -260,12 +260,12 @@ static int g_status = 0;
 
 template <int H, bool CONJ, int NZ>
 void run_col(float2* Q, const float2* R, int r_pitch, const float2* spec, const float2* tw, int h,
-             int W2, int rows, int cap) {
+             int W2, int rows, int nt, long long qts, long long rts, int cap) {
     using C = zf::ColCfg<H, NZ>;
-    int grid = (W2 + 1 + C::FPB - 1) / C::FPB;
+    int grid = (W2 + C::FPB) / C::FPB * nt;
     if (grid > cap) grid = cap;
     emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_col_fused<H, CONJ, NZ>, Q, R,
-               r_pitch, spec, tw, h, W2, rows, R != Q ? 1 : 0, &g_status);
+               r_pitch, spec, tw, h, W2, rows, R != Q ? 1 : 0, nt, qts, rts, &g_status);
 }
 template <int W2, int NZ>
 void run_r2c(const float* tm, float2* R, const float2* tw, int h, int w, int r_pitch,
@@ -287,43 +287,47 @@ void run_col_fwd(float2* spec, const float2* tw, int W2, int cap) {
 template <int W2>
 void run_c2r(const float2* Q, int H, float* out, int* arg, float* sum, float* sumsq,
              unsigned* peak, const float2* tw, int orows, int ocols, int tindex, int reset,
-             int cap) {
+             int nt, long long ots, int cap) {
     using C = zf::C2rCfg<W2>;
-    zf::CUtensorMap map{reinterpret_cast<const unsigned char*>(Q), H, W2, (long long)H * 8,
+    zf::CUtensorMap map{reinterpret_cast<const unsigned char*>(Q), H, W2 * nt, (long long)H * 8,
                         C::RPB, C::BOXK, 8};
-    int groups = (orows + C::RPB - 1) / C::RPB;
+    int groups = (orows + C::RPB - 1) / C::RPB * nt;
     int grid = groups < cap ? groups : cap;
     float* nf = nullptr;
     unsigned* np = nullptr;
     if (arg && sum)
         emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM,
                    zf::k_row_c2r<W2, zf::kRunningStats>, map, out, arg, sum, sumsq, np, tw, orows,
-                   ocols, ocols, tindex, reset, &g_status);
+                   ocols, ocols, tindex, reset, nt, ots, &g_status);
     else if (arg)
         emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_row_c2r<W2, zf::kRunningMax>,
-                   map, out, arg, nf, nf, np, tw, orows, ocols, ocols, tindex, reset, &g_status);
+                   map, out, arg, nf, nf, np, tw, orows, ocols, ocols, tindex, reset, nt, ots,
+                   &g_status);
     else if (peak)
         emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_row_c2r<W2, zf::kStorePeak>,
-                   map, out, (int*)nullptr, nf, nf, peak, tw, orows, ocols, ocols, 0, 0, &g_status);
+                   map, out, (int*)nullptr, nf, nf, peak, tw, orows, ocols, ocols, 0, 0, nt, ots,
+                   &g_status);
     else
         emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_row_c2r<W2, zf::kStoreMap>,
-                   map, out, (int*)nullptr, nf, nf, np, tw, orows, ocols, ocols, 0, 0, &g_status);
+                   map, out, (int*)nullptr, nf, nf, np, tw, orows, ocols, ocols, 0, 0, nt, ots,
+                   &g_status);
 }
 
 #define EMU_SIZES(X) X(64) X(128) X(256) X(512) X(2048) X(120) X(240)
 
 static void col(int H, bool conj, int nz, float2* Q, const float2* R, int rp, const float2* spec,
-                const float2* tw, int h, int W2, int rows, int cap) {
+                const float2* tw, int h, int W2, int rows, int cap, int nt = 1, long long qts = 0,
+                long long rts = 0) {
 #define X(N)                                                                                   \
     if (H == N) {                                                                              \
         if (conj) {                                                                            \
-            if (nz == 1) return run_col<N, true, 1>(Q, R, rp, spec, tw, h, W2, rows, cap);     \
-            if (nz == 2) return run_col<N, true, 2>(Q, R, rp, spec, tw, h, W2, rows, cap);     \
-            return run_col<N, true, 0>(Q, R, rp, spec, tw, h, W2, rows, cap);                  \
+            if (nz == 1) return run_col<N, true, 1>(Q, R, rp, spec, tw, h, W2, rows, nt, qts, rts, cap); \
+            if (nz == 2) return run_col<N, true, 2>(Q, R, rp, spec, tw, h, W2, rows, nt, qts, rts, cap); \
+            return run_col<N, true, 0>(Q, R, rp, spec, tw, h, W2, rows, nt, qts, rts, cap);  \
         }                                                                                      \
-        if (nz == 1) return run_col<N, false, 1>(Q, R, rp, spec, tw, h, W2, rows, cap);        \
-        if (nz == 2) return run_col<N, false, 2>(Q, R, rp, spec, tw, h, W2, rows, cap);        \
-        return run_col<N, false, 0>(Q, R, rp, spec, tw, h, W2, rows, cap);                     \
+        if (nz == 1) return run_col<N, false, 1>(Q, R, rp, spec, tw, h, W2, rows, nt, qts, rts, cap); \
+        if (nz == 2) return run_col<N, false, 2>(Q, R, rp, spec, tw, h, W2, rows, nt, qts, rts, cap); \
+        return run_col<N, false, 0>(Q, R, rp, spec, tw, h, W2, rows, nt, qts, rts, cap);     \
     }
     EMU_SIZES(X)
 #undef X
@@ -345,11 +349,11 @@ static void r2c(int W, int nz, const float* tm, float2* R, const float2* tw, int
 }
 static void c2r(int W, const float2* Q, int H, float* out, int* arg, float* sum, float* sumsq,
                 unsigned* peak, const float2* tw, int orows, int ocols, int tindex, int reset,
-                int cap) {
+                int cap, int nt = 1, long long ots = 0) {
 #define X(N)                                                                                    \
     if (W == N)                                                                                 \
         return run_c2r<N / 2>(Q, H, out, arg, sum, sumsq, peak, tw, orows, ocols, tindex, reset, \
-                              cap);
+                              nt, ots, cap);
     EMU_SIZES(X)
 #undef X
     std::fprintf(stderr, "unsupported W %d\n", W);
@@ -401,14 +405,15 @@ int main(int argc, char** argv) {
     }
     FILE* f = std::fopen(argv[1], "rb");
     if (!f) return 2;
-    int hd[13];
-    if (std::fread(hd, sizeof(int), 13, f) != 13) return 2;
+    int hd[14];
+    if (std::fread(hd, sizeof(int), 14, f) != 14) return 2;
     const int B = hd[0], sy = hd[1], sx = hd[2], H = hd[3], W = hd[4], oy = hd[5], ox = hd[6];
     const bool conj = hd[7] != 0;
     const int cap = hd[8], nz_col = hd[9], nz_row = hd[10], chunk = hd[11];
     const bool max_mode = hd[12] == 1 || hd[12] == 2;  // fold into running max / argmax maps
     const bool stats = hd[12] == 2;                    // ... and into sum / sum-of-squares maps
     const bool peaks_mode = hd[12] == 3;               // maps plus per-template peaks
+    const int group = max_mode ? 0 : hd[13];           // >= 2: batched groups
     const int W2 = W / 2;
     std::vector<float> tm((size_t)B * sy * sx);
     std::vector<float2> spec((size_t)(W2 + 1) * H);
@@ -421,7 +426,9 @@ int main(int argc, char** argv) {
     // after Q with pitch round_up(h, 2), else into rows [0, h) of Q.
     const long long h_pad = (sy + 1) / 2 * 2;
     const long long q_elems = (long long)H * W2, r_elems = (long long)W2 * h_pad;
-    std::vector<float4> ws_store((q_elems + (chunk > 0 ? chunk : 0) * r_elems + 1) / 2 + 1);
+    const long long ws_elems = group >= 2 ? group * q_elems
+                                          : q_elems + (chunk > 0 ? chunk : 0) * r_elems;
+    std::vector<float4> ws_store((ws_elems + 1) / 2 + 1);
     float2* Q = reinterpret_cast<float2*>(ws_store.data());
     float2* Rregion = Q + q_elems;
     std::vector<float> out((size_t)(max_mode ? 1 : B) * oy * ox);
@@ -432,8 +439,21 @@ int main(int argc, char** argv) {
     std::vector<unsigned> peak_keys(peaks_mode ? B : 0, 0u);
     auto twH = twiddles(H), twW = twiddles(W);
     const float scale = float(1.0 / (double(H) * double(W)));
+    // Batched groups: each template of a group in its own Q slice, rows
+    // first in rows [0, h) of the slice, one launch per kernel per group.
+    for (int t0 = 0; group >= 2 && t0 < B; t0 += group) {
+        const int n = B - t0 < group ? B - t0 : group;
+        r2c(W, nz_row, tm.data() + (size_t)t0 * sy * sx, Q, twW.data(), sy, sx, H, q_elems, n,
+            scale, cap);
+        col(H, conj, nz_col, Q, Q, H, spec.data(), twH.data(), sy, W2, oy, cap, n, q_elems,
+            q_elems);
+        // the tile map spans the whole group's slices, as on the device
+        c2r(W, Q, H, out.data() + (size_t)t0 * oy * ox, nullptr, nullptr, nullptr,
+            peaks_mode ? peak_keys.data() + t0 : nullptr, twW.data(), oy, ox, 0, 0, cap, n,
+            (long long)oy * ox);
+    }
     const int step = chunk > 0 ? chunk : 1;
-    for (int t0 = 0; t0 < B; t0 += step) {
+    for (int t0 = 0; group < 2 && t0 < B; t0 += step) {
         const int n = B - t0 < step ? B - t0 : step;
         if (chunk > 0)
             r2c(W, nz_row, tm.data() + (size_t)t0 * sy * sx, Rregion, twW.data(), sy, sx, (int)h_pad,

@@ -47,7 +47,7 @@ def nz_of(n, length):
 
 
 def run_emu(exe, tmp_path, B, sy, sx, H, W, conj, full, nz_col=None, nz_row=None, seed=0,
-            chunk=0, max_mode=False):
+            chunk=0, max_mode=False, group=0):
     rng = np.random.default_rng(seed)
     img = rng.standard_normal((H, W)).astype(np.float32)
     tm = rng.standard_normal((B, sy, sx)).astype(np.float32)
@@ -57,8 +57,8 @@ def run_emu(exe, tmp_path, B, sy, sx, H, W, conj, full, nz_col=None, nz_row=None
     nz_row = nz_of(W // 2, (sx + 1) // 2) if nz_row is None else nz_row
     fin, fout = str(tmp_path / "in.bin"), str(tmp_path / "out.bin")
     with open(fin, "wb") as f:
-        np.array([B, sy, sx, H, W, oy, ox, int(conj), 3, nz_col, nz_row, chunk, int(max_mode)],
-                 np.int32).tofile(f)
+        np.array([B, sy, sx, H, W, oy, ox, int(conj), 3, nz_col, nz_row, chunk, int(max_mode),
+                  group], np.int32).tofile(f)
         tm.tofile(f)
         spec.tofile(f)
     res = subprocess.run([exe, fin, fout], capture_output=True, text=True)
@@ -199,3 +199,22 @@ def test_emulated_random_shapes(emu, tmp_path, case):
                        seed=B + sy + sx)
     assert O.rel_l2(ref, out) < 1e-6
     assert O.max_abs_over_peak(ref, out) < 1e-5
+
+
+@pytest.mark.parametrize("case", [(5, 16, 16, 64, 64, True, True, 2), (3, 30, 45, 128, 256, False, False, 3),
+                                  (4, 9, 13, 120, 240, True, False, 4), (2, 100, 20, 2048, 64, True, True, 2)],
+                         ids=lambda c: str(c))
+def test_emulated_batched_groups(emu, tmp_path, case):
+    """Batched groups: one launch of each kernel for a group of templates,
+    each in its own Q slice; partial last group."""
+    B, sy, sx, H, W, conj, full, group = case
+    out, ref = run_emu(emu, tmp_path, B, sy, sx, H, W, conj, full, group=group)
+    assert O.rel_l2(ref, out) < 1e-6
+    assert O.max_abs_over_peak(ref, out) < 1e-5
+
+
+def test_emulated_batched_peaks(emu, tmp_path):
+    B, H, W = 5, 64, 256
+    (out, peaks), ref = run_emu(emu, tmp_path, B, 12, 10, H, W, True, False, max_mode=3, group=2)
+    assert O.rel_l2(ref, out) < 1e-6
+    assert np.array_equal(peaks, out.reshape(B, -1).max(axis=1))

@@ -185,7 +185,9 @@ def test_bounded_wait_reports_timeout_and_context_survives():
 @pytest.mark.parametrize("H,h,B", [(4096, 256, 5), (1024, 100, 7), (3840, 384, 3)])
 def test_chunked_and_in_place_layouts_agree(H, h, B):
     """Workspaces large enough for several templates' rows (chunked row
-    launches) give bit-identical results to the minimal in-place workspace."""
+    launches) or, for small images, several whole intermediates (batched
+    groups: one launch per kernel for a group of templates) give bit-identical
+    results to the minimal in-place workspace."""
     from zipfft_b200 import _lib
 
     _, tm, spec = make_inputs(B, h, h, H, H, seed=H + B)
@@ -272,3 +274,33 @@ def test_random_shapes_match_oracle(case):
     out = capi_corr(tm, spec, H, W, full, conj)
     ref = O.padded_corr2d_f64(tm.numpy(), spec.numpy(), H, W, conj, full)
     assert_parity(ref, out, what=str(case))
+
+
+@pytest.mark.parametrize("B,sy,sx,H,W,full,conj", [(11, 128, 128, 1024, 1024, True, True),
+                                                   (7, 48, 33, 512, 256, False, False),
+                                                   (9, 20, 30, 120, 480, False, True)])
+def test_batched_groups_agree_with_per_template_path(B, sy, sx, H, W, full, conj):
+    """Small images with a (B, H, W/2+1) workspace run as batched groups;
+    results equal the one-slice workspace's per-template launches bit for bit
+    (and the oracle), peaks included."""
+    import zipfft
+    from zipfft_b200 import _lib
+
+    _, tm, spec = make_inputs(B, sy, sx, H, W, seed=B * 3 + sy)
+    dev = torch.device("cuda", 0)
+    nmin = _lib.load().zfft_workspace_bytes(H, W) // 8
+    a = capi_corr(tm, spec, H, W, full, conj, ws=torch.empty(nmin, dtype=torch.complex64,
+                                                             device=dev))
+    big = torch.empty((B, H, W // 2 + 1), dtype=torch.complex64, device=dev)
+    b = capi_corr(tm, spec, H, W, full, conj, ws=big)
+    assert np.array_equal(a, b)
+    ref = O.padded_corr2d_f64(tm.numpy(), spec.numpy(), H, W, conj, full)
+    assert_parity(ref, b, what="batched groups")
+    if conj:
+        oy, ox = O.out_shape(sy, sx, H, W, full)
+        out = torch.empty((B, oy, ox), device=dev)
+        peaks = torch.empty(B, device=dev)
+        zipfft.padded_rconv2d.corr(tm.to(dev), big, spec.to(dev), out, H, W, peaks=peaks)
+        torch.cuda.synchronize()
+        assert np.array_equal(out.cpu().numpy(), b)
+        assert torch.equal(peaks, out.reshape(B, -1).amax(dim=1))

@@ -34,6 +34,10 @@ namespace {
 constexpr int kVersion = 300;  // 0.3.0
 constexpr int kMaxDevices = 64;
 constexpr int kMaxChunk = 32;  // templates per row-r2c launch
+// Batched groups (small images): the intermediates of one group, written by
+// one column launch and read by one inverse-row launch, stay within this
+// much of the 126 MB L2.
+constexpr long long kBatchL2Bytes = 48ll << 20;
 
 thread_local std::string g_last_error;
 
@@ -196,13 +200,15 @@ void timer_close(int stage, int start, cudaStream_t s) {
 }
 
 using ColFn = cudaError_t (*)(float2*, const float2*, int, const float2*, const float2*, int, int,
-                              int, bool, int, bool, int*, int, cudaStream_t);
+                              int, bool, int, bool, int, long long, long long, int*, int,
+                              cudaStream_t);
 using R2cFn = cudaError_t (*)(const float*, float2*, const float2*, int, int, int, long long, int,
                               float, int, int, cudaStream_t);
 using ColFwdFn = cudaError_t (*)(float2*, const float2*, int, int*, int, cudaStream_t);
-using QmapFn = cudaError_t (*)(const float2*, int, CUtensorMap*);
+using QmapFn = cudaError_t (*)(const float2*, int, int, CUtensorMap*);
 using C2rFn = cudaError_t (*)(const CUtensorMap*, float*, int*, float*, float*, unsigned*,
-                              const float2*, int, int, int, int, int, int*, int, cudaStream_t);
+                              const float2*, int, int, int, int, int, int, long long, int*, int,
+                              cudaStream_t);
 
 ColFn col_fn(int n) {
 #define ZF_X(N) \
@@ -368,10 +374,24 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
     }
     float2* Rregion = Q + q_elems;
 
+    // Batched groups: when at least two whole Q slices fit in the workspace
+    // and together within kBatchL2Bytes, the templates of a group go through
+    // each kernel in one launch, each in its own slice (its row spectra first
+    // in rows [0, h) of the slice).  Maps only: the running maps need the
+    // templates one after another.
+    long long group = 0;
+    if (!arg && batch > 1) {
+        const long long fit_ws = (long long)(ws_bytes / sizeof(float2)) / q_elems;
+        const long long fit_l2 = kBatchL2Bytes / (q_elems * (long long)sizeof(float2));
+        group = batch;
+        if (fit_ws < group) group = fit_ws;
+        if (fit_l2 < group) group = fit_l2;
+    }
+
     CUtensorMap qmap;
-    e = qmap_fn(W)(Q, H, &qmap);
+    e = qmap_fn(W)(Q, H, group >= 2 ? (int)group : 1, &qmap);
     if (e != cudaSuccess) return cuda_fail(e, "encoding the intermediate's tensor map");
-    trace("tensor map encoded; chunk %d", chunk);
+    trace("tensor map encoded; chunk %d group %lld", chunk, group);
     ColFn col = col_fn(H);
     R2cFn r2c = r2c_fn(W);
     C2rFn c2r = c2r_fn(W);
@@ -382,8 +402,32 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
         e = cudaMemsetAsync(peaks, 0, sizeof(float) * (size_t)batch, s);
         if (e != cudaSuccess) return cuda_fail(e, "clearing the peaks");
     }
+    if (group >= 2) {
+        for (int t0 = 0; t0 < batch; t0 += (int)group) {
+            const int n = batch - t0 < group ? batch - t0 : (int)group;
+            int m = timer_mark(s);
+            e = r2c(input + (size_t)t0 * sy * sx, Q, twW, sy, sx, H, q_elems, n, scale, nz_row,
+                    device, s);
+            if (e != cudaSuccess) return cuda_fail(e, "row r2c launch");
+            timer_close(0, m, s);
+            if ((e = trace_sync(s, "k_row_r2c group", t0)) != cudaSuccess) return cuda_fail(e, "k_row_r2c");
+            m = timer_mark(s);
+            e = col(Q, Q, H, spec, twH, sy, W2, oy, conj, nz_col, false, n, q_elems, q_elems, status,
+                    device, s);
+            if (e != cudaSuccess) return cuda_fail(e, "column launch");
+            timer_close(1, m, s);
+            if ((e = trace_sync(s, "k_col_fused group", t0)) != cudaSuccess) return cuda_fail(e, "k_col_fused");
+            m = timer_mark(s);
+            e = c2r(&qmap, output + (size_t)t0 * oy * ox, nullptr, nullptr, nullptr,
+                    peak_keys ? peak_keys + t0 : nullptr, twW, oy, ox, ox, 0, 0, n,
+                    (long long)oy * ox, status, device, s);
+            if (e != cudaSuccess) return cuda_fail(e, "row c2r launch");
+            timer_close(2, m, s);
+            if ((e = trace_sync(s, "k_row_c2r group", t0)) != cudaSuccess) return cuda_fail(e, "k_row_c2r");
+        }
+    }
     const int step = chunk > 0 ? chunk : 1;
-    for (int t0 = 0; t0 < batch; t0 += step) {
+    for (int t0 = 0; group < 2 && t0 < batch; t0 += step) {
         const int n = batch - t0 < step ? batch - t0 : step;
         int m = -1;
         if (chunk > 0) {
@@ -409,18 +453,19 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
                 if ((e = trace_sync(s, "k_row_r2c", t)) != cudaSuccess) return cuda_fail(e, "k_row_r2c");
             }
             m = timer_mark(s);
-            e = col(Q, Rt, r_pitch, spec, twH, sy, W2, oy, conj, nz_col, chunk > 0, status, device, s);
+            e = col(Q, Rt, r_pitch, spec, twH, sy, W2, oy, conj, nz_col, chunk > 0, 1, 0, 0, status,
+                    device, s);
             if (e != cudaSuccess) return cuda_fail(e, "column launch");
             timer_close(1, m, s);
             if ((e = trace_sync(s, "k_col_fused", t)) != cudaSuccess) return cuda_fail(e, "k_col_fused");
             m = timer_mark(s);
             if (arg)
                 e = c2r(&qmap, output, arg, sum, sumsq, nullptr, twW, oy, ox, ox, tindex_base + t,
-                        (reset && t == 0) ? 1 : 0, status, device, s);
+                        (reset && t == 0) ? 1 : 0, 1, 0, status, device, s);
             else
                 e = c2r(&qmap, output + (size_t)t * oy * ox, nullptr, nullptr, nullptr,
-                        peak_keys ? peak_keys + t : nullptr, twW, oy, ox, ox, 0, 0, status, device,
-                        s);
+                        peak_keys ? peak_keys + t : nullptr, twW, oy, ox, ox, 0, 0, 1, 0, status,
+                        device, s);
             if (e != cudaSuccess) return cuda_fail(e, "row c2r launch");
             timer_close(2, m, s);
             if ((e = trace_sync(s, "k_row_c2r", t)) != cudaSuccess) return cuda_fail(e, "k_row_c2r");

@@ -87,7 +87,8 @@ cudaError_t r2c_t(const float* tmpl, float2* R, const float2* tw, int h, int w, 
 
 template <int H, bool CONJ, int NZ>
 cudaError_t col_t(float2* Q, const float2* R, int r_pitch, const float2* spec, const float2* tw,
-                  int h, int W2, int store_rows, bool discard_r, int* status, int device,
+                  int h, int W2, int store_rows, bool discard_r, int ntemplates,
+                  long long q_tstride, long long r_tstride, int* status, int device,
                   cudaStream_t s) {
     using C = ColCfg<H, NZ>;
     static KernelState st;
@@ -95,9 +96,10 @@ cudaError_t col_t(float2* Q, const float2* R, int r_pitch, const float2* spec, c
     int cap = 0;
     cudaError_t e = configure(kernel, st, C::SMEM, C::THREADS, device, &cap);
     if (e != cudaSuccess) return e;
-    const int grid = min_int((W2 + 1 + C::FPB - 1) / C::FPB, cap);
+    const long long units = (long long)((W2 + C::FPB) / C::FPB) * ntemplates;
+    const int grid = (int)(units < cap ? units : cap);
     return launch_pdl(kernel, dim3(grid), C::THREADS, C::SMEM, s, Q, R, r_pitch, spec, tw, h, W2,
-                      store_rows, discard_r ? 1 : 0, status);
+                      store_rows, discard_r ? 1 : 0, ntemplates, q_tstride, r_tstride, status);
 }
 
 template <int H>
@@ -116,17 +118,19 @@ cudaError_t col_fwd_t(float2* spec, const float2* tw, int W2, int* status, int d
 template <int W2, int MODE>
 cudaError_t c2r_t(const CUtensorMap* qmap, float* out, int* arg, float* sum, float* sumsq,
                   unsigned* peak, const float2* tw, int out_rows, int out_cols, int out_pitch,
-                  int tindex, int reset, int* status, int device, cudaStream_t s) {
+                  int tindex, int reset, int ntemplates, long long out_tstride, int* status,
+                  int device, cudaStream_t s) {
     using C = C2rCfg<W2>;
     static KernelState st;
     auto kernel = k_row_c2r<W2, MODE>;
     int cap = 0;
     cudaError_t e = configure(kernel, st, C::SMEM, C::THREADS, device, &cap);
     if (e != cudaSuccess) return e;
-    const int groups = (out_rows + C::RPB - 1) / C::RPB;
-    const int grid = min_int(groups, cap);
+    const long long units = (long long)((out_rows + C::RPB - 1) / C::RPB) * ntemplates;
+    const int grid = (int)(units < cap ? units : cap);
     return launch_pdl(kernel, dim3(grid), C::THREADS, C::SMEM, s, *qmap, out, arg, sum, sumsq, peak,
-                      tw, out_rows, out_cols, out_pitch, tindex, reset, status);
+                      tw, out_rows, out_cols, out_pitch, tindex, reset, ntemplates, out_tstride,
+                      status);
 }
 
 // The pruned starts (nz = 1, 2) are instantiated for sizes >= 1024, where
@@ -153,10 +157,12 @@ cudaError_t ZF_CAT(launch_row_r2c_, ZF_SIZE)(const float* tmpl, float2* R, const
 cudaError_t ZF_CAT(launch_col_, ZF_SIZE)(float2* Q, const float2* R, int r_pitch,
                                          const float2* spec, const float2* tw, int h, int W2,
                                          int store_rows, bool conj, int nz, bool discard_r,
+                                         int ntemplates, long long q_tstride, long long r_tstride,
                                          int* status, int device, cudaStream_t s) {
     constexpr int H = ZF_SIZE;
-#define ZF_COL(CJ, NZV) \
-    col_t<H, CJ, NZV>(Q, R, r_pitch, spec, tw, h, W2, store_rows, discard_r, status, device, s)
+#define ZF_COL(CJ, NZV)                                                                       \
+    col_t<H, CJ, NZV>(Q, R, r_pitch, spec, tw, h, W2, store_rows, discard_r, ntemplates,      \
+                      q_tstride, r_tstride, status, device, s)
     if constexpr (kPruned) {
         if (nz == 1) return conj ? ZF_COL(true, 1) : ZF_COL(false, 1);
         if (nz == 2) return conj ? ZF_COL(true, 2) : ZF_COL(false, 2);
@@ -170,30 +176,37 @@ cudaError_t ZF_CAT(launch_col_fwd_, ZF_SIZE)(float2* spec, const float2* tw, int
     return col_fwd_t<ZF_SIZE>(spec, tw, W2, status, device, s);
 }
 
-cudaError_t ZF_CAT(make_qmap_, ZF_SIZE)(const float2* Q, int H, CUtensorMap* map) {
+cudaError_t ZF_CAT(make_qmap_, ZF_SIZE)(const float2* Q, int H, int ntemplates, CUtensorMap* map) {
     using C = C2rCfg<ZF_SIZE / 2>;
-    // Q is column-major: dim 0 = rows y (H, contiguous), dim 1 = packed columns.
-    return encode_tensor_map_2d(map, Q, (unsigned long long)H, (unsigned long long)(ZF_SIZE / 2),
+    // Q is column-major: dim 0 = rows y (H, contiguous), dim 1 = packed columns
+    // of ntemplates consecutive slices.
+    return encode_tensor_map_2d(map, Q, (unsigned long long)H,
+                                (unsigned long long)(ZF_SIZE / 2) * (unsigned long long)ntemplates,
                                 (unsigned long long)H * 8ull, C::RPB, C::BOXK);
 }
 
 cudaError_t ZF_CAT(launch_row_c2r_, ZF_SIZE)(const CUtensorMap* qmap, float* out, int* arg,
                                              float* sum, float* sumsq, unsigned* peak,
                                              const float2* tw, int out_rows, int out_cols,
-                                             int out_pitch, int tindex, int reset, int* status,
-                                             int device, cudaStream_t s) {
+                                             int out_pitch, int tindex, int reset, int ntemplates,
+                                             long long out_tstride, int* status, int device,
+                                             cudaStream_t s) {
     constexpr int W2 = ZF_SIZE / 2;
+    if (arg != nullptr && ntemplates != 1) return cudaErrorInvalidValue;
     if (arg != nullptr && sum != nullptr)
         return c2r_t<W2, kRunningStats>(qmap, out, arg, sum, sumsq, nullptr, tw, out_rows,
-                                        out_cols, out_pitch, tindex, reset, status, device, s);
+                                        out_cols, out_pitch, tindex, reset, 1, 0, status, device,
+                                        s);
     if (arg != nullptr)
         return c2r_t<W2, kRunningMax>(qmap, out, arg, nullptr, nullptr, nullptr, tw, out_rows,
-                                      out_cols, out_pitch, tindex, reset, status, device, s);
+                                      out_cols, out_pitch, tindex, reset, 1, 0, status, device, s);
     if (peak != nullptr)
         return c2r_t<W2, kStorePeak>(qmap, out, nullptr, nullptr, nullptr, peak, tw, out_rows,
-                                     out_cols, out_pitch, 0, 0, status, device, s);
+                                     out_cols, out_pitch, 0, 0, ntemplates, out_tstride, status,
+                                     device, s);
     return c2r_t<W2, kStoreMap>(qmap, out, nullptr, nullptr, nullptr, nullptr, tw, out_rows,
-                                out_cols, out_pitch, 0, 0, status, device, s);
+                                out_cols, out_pitch, 0, 0, ntemplates, out_tstride, status, device,
+                                s);
 }
 
 }  // namespace zf

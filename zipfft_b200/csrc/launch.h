@@ -14,12 +14,14 @@ namespace zf {
 // kx * r_pitch + n.  nz: 1 or 2 when the template row fits the first 1 or 2
 // stage-0 inputs of every butterfly, else 0.
 // Column pass of an H-row image: forward FFT of the h rows of R, product with
-// the spectrum, inverse FFT, first store_rows rows of Q stored.
+// the spectrum, inverse FFT, first store_rows rows of Q stored; ntemplates
+// templates, template j's Q / R at Q + j q_tstride / R + j r_tstride.
 // Image spectrum column pass: in place over the W2 packed columns (pitch H)
 // that the row r2c wrote into spec, and the split of packed column 0 into
 // rows 0 and W2.
-// Row c2r: the Q tile map comes from make_qmap_<W> (same W); out_rows rows of
-// out_cols values at out_pitch.  arg == nullptr: store the map into out;
+// Row c2r: the Q tile map comes from make_qmap_<W> (same W, covering
+// ntemplates consecutive Q slices); out_rows rows of out_cols values at
+// out_pitch, template j's map at out + j out_tstride.  arg == nullptr: store the map into out;
 // otherwise fold it into the running max (out) / argmax (arg) maps with
 // template index tindex (reset: overwrite instead of compare), and with sum
 // != nullptr also add it and its square to the sum / sumsq maps.  With
@@ -31,14 +33,16 @@ namespace zf {
                                    int nz, int device, cudaStream_t s);                          \
     cudaError_t launch_col_##N(float2* Q, const float2* R, int r_pitch, const float2* spec,      \
                                const float2* tw, int h, int W2, int store_rows, bool conj, int nz, \
-                               bool discard_r, int* status, int device, cudaStream_t s);         \
+                               bool discard_r, int ntemplates, long long q_tstride,              \
+                               long long r_tstride, int* status, int device, cudaStream_t s);    \
     cudaError_t launch_col_fwd_##N(float2* spec, const float2* tw, int W2, int* status,         \
                                    int device, cudaStream_t s);                                  \
-    cudaError_t make_qmap_##N(const float2* Q, int H, CUtensorMap* map);                        \
+    cudaError_t make_qmap_##N(const float2* Q, int H, int ntemplates, CUtensorMap* map);        \
     cudaError_t launch_row_c2r_##N(const CUtensorMap* qmap, float* out, int* arg, float* sum,   \
                                    float* sumsq, unsigned* peak, const float2* tw, int out_rows, \
                                    int out_cols, int out_pitch, int tindex, int reset,           \
-                                   int* status, int device, cudaStream_t s);
+                                   int ntemplates, long long out_tstride, int* status,           \
+                                   int device, cudaStream_t s);
 ZF_FOR_EACH_FFT_SIZE(ZF_DECL)
 #undef ZF_DECL
 

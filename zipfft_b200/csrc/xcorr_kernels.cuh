@@ -206,7 +206,8 @@ template <int H, bool CONJ, int NZ>
 __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
     k_col_fused(float2* __restrict__ Q, const float2* __restrict__ R, int r_pitch,
                 const float2* __restrict__ spec, const float2* __restrict__ twH, int h, int W2,
-                int store_rows, int discard_r, int* __restrict__ status) {
+                int store_rows, int discard_r, int ntemplates, long long q_tstride,
+                long long r_tstride, int* __restrict__ status) {
     using C = ColCfg<H, NZ>;
     using F = Stockham<H, C::T, false, false>;
     using I = Stockham<H, C::T, true, true>;
@@ -244,7 +245,10 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
     pdl_wait_prerequisites();
 
     const uint32_t r_bytes = (uint32_t)round_up(h, 2) * 8u;
-    const int stride = gridDim.x * C::FPB;
+    // Units (template, column group): ntemplates templates of W2 + 1 virtual
+    // columns each, template j's Q and R at Q + j q_tstride, R + j r_tstride.
+    const int cgroups = (W2 + C::FPB) / C::FPB;
+    const int units = cgroups * ntemplates;
     // L2 policy: template columns stream through (read once); the spectrum,
     // read once per template but by every template, keeps the normal policy
     // (some of it then survives in L2 for the next template: measured faster
@@ -254,8 +258,10 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
     const uint64_t pol_spec = l2_evict_normal();
     const uint64_t pol_keep = l2_evict_last();
 
-    // Thread 0 fetches the spectrum and template columns of group vc0 into buffer b.
-    auto issue = [&](int b, int vc0) {
+    // Thread 0 fetches the spectrum and template columns of unit u into buffer b.
+    auto issue = [&](int b, int u) {
+        const int tj = u / cgroups, vc0 = (u - tj * cgroups) * C::FPB;
+        const float2* Rj = R + tj * r_tstride;
         uint32_t bytes = 0;
         for (int j = 0; j < C::FPB; ++j)
             if (vc0 + j <= W2) bytes += H * 8u + r_bytes;
@@ -266,19 +272,22 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
             tma_load_1d(sbase + (b * C::FPB + j) * C::SB, spec + (size_t)vc * H, H * 8u, &mbar[b],
                         pol_spec);
             const int rc = vc == W2 ? 0 : vc;
-            tma_load_1d(rbase + (b * C::FPB + j) * C::RB, R + (size_t)rc * r_pitch, r_bytes,
+            tma_load_1d(rbase + (b * C::FPB + j) * C::RB, Rj + (size_t)rc * r_pitch, r_bytes,
                         &mbar[b], pol_stream);
         }
     };
 
-    int vc0 = blockIdx.x * C::FPB;
-    if (tid == 0 && vc0 <= W2) issue(0, vc0);
-    for (int it = 0; vc0 <= W2; ++it, vc0 += stride) {
+    int u = blockIdx.x;
+    if (tid == 0 && u < units) issue(0, u);
+    for (int it = 0; u < units; ++it, u += gridDim.x) {
         const int b = it & 1;
         const uint32_t parity = (it >> 1) & 1;
+        const int tj = u / cgroups, vc0 = (u - tj * cgroups) * C::FPB;
+        float2* Qj = Q + tj * q_tstride;
+        const float2* Rj = R + tj * r_tstride;
         // The other buffer was last read before this iteration's barriers.
-        const bool more = vc0 + stride <= W2;
-        if (tid == 0 && more) issue(b ^ 1, vc0 + stride);
+        const bool more = u + (int)gridDim.x < units;
+        if (tid == 0 && more) issue(b ^ 1, u + gridDim.x);
         const bool ok = mbar_wait_bounded(&mbar[b], parity);
         // The previous column's bulk store must have read the exchange buffer
         // before this column writes it (the barrier below publishes that).
@@ -301,7 +310,7 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
         // once copied: drop its whole 128-byte lines from L2 without write-back.
         // Packed column 0 is read by two column kinds and is kept.
         if (discard_r && active && mode == 0) {
-            const char* c0 = reinterpret_cast<const char*>(R + (size_t)vc * r_pitch);
+            const char* c0 = reinterpret_cast<const char*>(Rj + (size_t)vc * r_pitch);
             const size_t lo = (reinterpret_cast<size_t>(c0) + 127) & ~size_t(127);
             const size_t hi = (reinterpret_cast<size_t>(c0) + r_bytes) & ~size_t(127);
             for (size_t a = lo + (size_t)t * 128; a < hi; a += (size_t)C::T * 128)
@@ -373,7 +382,7 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
                 __syncthreads();
                 if (tid == 0) {
                     const int rows = store_rows >= H ? H : ((store_rows + 1) & ~1);
-                    tma_store_1d(Q + (size_t)vc * H, xbuf, (uint32_t)rows * 8u, pol_keep);
+                    tma_store_1d(Qj + (size_t)vc * H, xbuf, (uint32_t)rows * 8u, pol_keep);
                     bulk_commit();
                 }
                 continue;
@@ -382,7 +391,7 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
         if (active) {
             const bool full = store_rows >= H;
             if (mode == 0) {
-                float2* dst = Q + (size_t)vc * H;
+                float2* dst = Qj + (size_t)vc * H;
 #pragma unroll
                 for (int q = 0; q < I::bpt(I::S - 1); ++q) {
                     const int bb = t + q * C::T;
@@ -395,7 +404,7 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
                     }
                 }
             } else {
-                float* dstf = reinterpret_cast<float*>(Q) + (mode == 2 ? 1 : 0);
+                float* dstf = reinterpret_cast<float*>(Qj) + (mode == 2 ? 1 : 0);
 #pragma unroll
                 for (int q = 0; q < I::bpt(I::S - 1); ++q) {
                     const int bb = t + q * C::T;
@@ -602,7 +611,8 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     k_row_c2r(const __grid_constant__ CUtensorMap qmap, float* __restrict__ out,
               int* __restrict__ arg, float* __restrict__ sum, float* __restrict__ sumsq,
               unsigned* __restrict__ peak, const float2* __restrict__ twW, int out_rows,
-              int out_cols, int out_pitch, int tindex, int reset, int* __restrict__ status) {
+              int out_cols, int out_pitch, int tindex, int reset, int ntemplates,
+              long long out_tstride, int* __restrict__ status) {
     using C = C2rCfg<W2>;
     using I = Stockham<W2, C::T, true, false>;
     static_assert(I::S >= 2, "row FFT needs at least two stages");
@@ -638,29 +648,36 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     // Q comes from the previous kernel.
     pdl_wait_prerequisites();
 
+    // Units (template, row group): template j's Q is columns [j W2, (j+1) W2)
+    // of the tile map, its map out + j out_tstride and its peak peak[j]
+    // (the running-map modes take one template per launch).
     const int ngroups = (out_rows + C::RPB - 1) / C::RPB;
+    const int units = ngroups * ntemplates;
 
     // L2 policy: Q lines stay resident (the next template's column pass
     // overwrites them there without a DRAM round trip); output rows stream out.
     const uint64_t pol_keep = l2_evict_last();
     const uint64_t pol_stream = l2_evict_first();
-    auto issue = [&](int b, int grp) {
+    auto issue = [&](int b, int u) {
+        const int tj = u / ngroups, grp = u - tj * ngroups;
         mbar_arrive_expect_tx(&mbar[b], (uint32_t)(W2 * C::RPB * 8));
         for (int k0 = 0; k0 < W2; k0 += C::BOXK)
-            tma_load_2d(qbase + b * C::QB + k0 * C::RPB, &qmap, grp * C::RPB, k0, &mbar[b],
-                        pol_keep);
+            tma_load_2d(qbase + b * C::QB + k0 * C::RPB, &qmap, grp * C::RPB, tj * W2 + k0,
+                        &mbar[b], pol_keep);
     };
 
     // Output rows leave through per-thread stores: staging them for bulk
     // stores needs one more block barrier per group, which cost more than the
     // store-queue stalls it removed.
-    int grp = blockIdx.x;
-    if (tid == 0 && grp < ngroups) issue(0, grp);
-    for (int it = 0; grp < ngroups; ++it, grp += gridDim.x) {
+    int u = blockIdx.x;
+    if (tid == 0 && u < units) issue(0, u);
+    for (int it = 0; u < units; ++it, u += gridDim.x) {
+        const int tj = u / ngroups, grp = u - tj * ngroups;
+        float* outj = out + tj * out_tstride;
         const int b = it & 1;
         const uint32_t parity = (it >> 1) & 1;
-        const bool more = grp + (int)gridDim.x < ngroups;
-        if (tid == 0 && more) issue(b ^ 1, grp + gridDim.x);
+        const bool more = u + (int)gridDim.x < units;
+        if (tid == 0 && more) issue(b ^ 1, u + gridDim.x);
         if constexpr (MODE != kStoreMap) {
             // The maps this group's epilogue reads: into L2 while the group
             // is transformed (whole 16-byte chunks inside each row only).
@@ -668,7 +685,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                 for (int r = 0; r < C::RPB; ++r) {
                     const int yy = grp * C::RPB + r;
                     if (yy >= out_rows) break;
-                    prefetch_row(out + (size_t)yy * out_pitch, out_cols);
+                    prefetch_row(outj + (size_t)yy * out_pitch, out_cols);
                     if constexpr (MODE == kRunningStats) {
                         prefetch_row(sum + (size_t)yy * out_pitch, out_cols);
                         prefetch_row(sumsq + (size_t)yy * out_pitch, out_cols);
@@ -713,7 +730,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
         const int y = grp * C::RPB + g;
         float pk = -INFINITY;  // kStorePeak: this thread's largest stored value
         if (y < out_rows) {
-            float* orow = out + (size_t)y * out_pitch;
+            float* orow = outj + (size_t)y * out_pitch;
             // Element m holds outputs 2m, 2m+1: one 8-byte access where the
             // row is 8-byte aligned and both lie inside the crop.  With an odd
             // pitch every other row qualifies.
@@ -871,7 +888,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
             // atomic per warp.
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) pk = fmaxf(pk, __shfl_xor_sync(0xffffffffu, pk, o));
-            if ((tid & 31) == 0) atomicMax(peak, ordered_key(pk));
+            if ((tid & 31) == 0) atomicMax(peak + tj, ordered_key(pk));
         }
     }
 }
