@@ -6,7 +6,8 @@
 // formulation (Stockham 1966; Govindaraju et al., SC'08) with FP32 arithmetic on
 // the CUDA cores:
 //
-//   * an N-point transform is split into stages of radix 16, 8, 4, 2, 5 and 3;
+//   * an N-point transform is split into stages of radix 16, 8, 4, 2, 15, 5 and
+//     3 (15 as a prime-factor 3 x 5 butterfly);
 //   * every stage runs N/R independent radix-R butterflies held in registers;
 //   * stages exchange data through one padded shared-memory buffer;
 //   * input and output are both in natural order, so a forward transform's last
@@ -278,9 +279,38 @@ ZF_HD void dft5(float2* v) {
     v[3] = c_sub(m2, r2);
 }
 
+// 15-point DFT by the prime-factor (Good-Thomas) algorithm, 15 = 3 x 5 with
+// coprime factors: the inputs x[(5 n1 + 3 n2) mod 15] form a 3 x 5 array whose
+// columns take 3-point and whose rows take 5-point DFTs, with no twiddles in
+// between, and X[(10 k1 + 6 k2) mod 15] = Y[k1][k2] (10 = 5 (5^-1 mod 3),
+// 6 = 3 (3^-1 mod 5)).
+template <bool INV>
+ZF_HD void dft15(float2* v) {
+    float2 a[3][5];
+#pragma unroll
+    for (int n1 = 0; n1 < 3; ++n1) {
+#pragma unroll
+        for (int n2 = 0; n2 < 5; ++n2) a[n1][n2] = v[(5 * n1 + 3 * n2) % 15];
+    }
+#pragma unroll
+    for (int n2 = 0; n2 < 5; ++n2) {
+        float2 c[3] = {a[0][n2], a[1][n2], a[2][n2]};
+        dft3<INV>(c);
+#pragma unroll
+        for (int k1 = 0; k1 < 3; ++k1) a[k1][n2] = c[k1];
+    }
+#pragma unroll
+    for (int k1 = 0; k1 < 3; ++k1) dft5<INV>(a[k1]);
+#pragma unroll
+    for (int k1 = 0; k1 < 3; ++k1) {
+#pragma unroll
+        for (int k2 = 0; k2 < 5; ++k2) v[(10 * k1 + 6 * k2) % 15] = a[k1][k2];
+    }
+}
+
 template <int R, bool INV>
 ZF_HD void dft(float2* v) {
-    static_assert(R == 2 || R == 3 || R == 4 || R == 5 || R == 8 || R == 16, "radix");
+    static_assert(R == 2 || R == 3 || R == 4 || R == 5 || R == 8 || R == 15 || R == 16, "radix");
     if constexpr (R == 2) {
         dft2<INV>(v[0], v[1]);
     } else if constexpr (R == 3) {
@@ -291,6 +321,8 @@ ZF_HD void dft(float2* v) {
         dft5<INV>(v);
     } else if constexpr (R == 8) {
         dft8<INV>(v);
+    } else if constexpr (R == 15) {
+        dft15<INV>(v);
     } else {
         dft16<INV>(v);
     }
@@ -298,7 +330,7 @@ ZF_HD void dft(float2* v) {
 
 // ---------------------------------------------------------------------------
 // Stockham plan: N = product of radices, largest first (16s, then the left-over
-// power of two, then 5s, then 3s).
+// power of two, then 15s, 5s and 3s; 16 x 16 x 15 is ordered 16, 15, 16).
 // ---------------------------------------------------------------------------
 struct PlanInfo {
     int S;
@@ -325,6 +357,10 @@ constexpr PlanInfo make_plan(int n) {
         pow2 /= 16;
     }
     if (pow2 > 1) p.R[p.S++] = pow2;  // 8, 4 or 2
+    while (n % 15 == 0) {  // a 3 and a 5 together: one prime-factor radix-15 stage
+        p.R[p.S++] = 15;
+        n /= 15;
+    }
     while (n % 5 == 0) {
         p.R[p.S++] = 5;
         n /= 5;
@@ -332,6 +368,12 @@ constexpr PlanInfo make_plan(int n) {
     while (n % 3 == 0) {
         p.R[p.S++] = 3;
         n /= 3;
+    }
+    // 16, 16, 15 -> 16, 15, 16: a palindromic plan, whose reversed inverse
+    // shares the forward transform's twiddles.
+    if (p.S == 3 && p.R[0] == 16 && p.R[1] == 16 && p.R[2] == 15) {
+        p.R[1] = 15;
+        p.R[2] = 16;
     }
     return p;
 }
