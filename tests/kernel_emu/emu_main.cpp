@@ -9,7 +9,8 @@
 //
 // Usage: zf_emu <in.bin> <out.bin>, or zf_emu spectrum <in.bin> <out.bin>
 //   in.bin : int32 header {B, sy, sx, H, W, oy, ox, conj, grid_cap, nz_col,
-//            nz_row, chunk, max_mode, group}, float32 templates [B][sy][sx],
+//            nz_row, chunk, max_mode, group (+ 1 << 16: workspace filled with
+//            NaN first)}, float32 templates [B][sy][sx],
 //            complex64 spectrum [W/2+1][H]
 //   out.bin: float32 [B][oy][ox] maps, or with max_mode the float32 [oy][ox]
 //            running maximum and int32 [oy][ox] argmax over the templates,
@@ -303,14 +304,24 @@ void run_c2r(const float2* Q, int H, float* out, int* arg, float* sum, float* su
         emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_row_c2r<W2, zf::kRunningMax>,
                    map, out, arg, nf, nf, np, tw, orows, ocols, ocols, tindex, reset, nt, ots,
                    &g_status);
-    else if (peak)
-        emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_row_c2r<W2, zf::kStorePeak>,
-                   map, out, (int*)nullptr, nf, nf, peak, tw, orows, ocols, ocols, 0, 0, nt, ots,
-                   &g_status);
+    else if (ocols == 2 * W2 && reinterpret_cast<uintptr_t>(out) % 8 == 0 && ots % 2 == 0) {
+        // full aligned maps: the W/2-point form, as the library launches it
+        if (peak)
+            emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM,
+                       zf::k_row_c2r<W2, zf::kStorePeak>, map, out, (int*)nullptr, nf, nf, peak, tw,
+                       orows, ocols, ocols, 0, 0, nt, ots, &g_status);
+        else
+            emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM,
+                       zf::k_row_c2r<W2, zf::kStoreMap>, map, out, (int*)nullptr, nf, nf, np, tw,
+                       orows, ocols, ocols, 0, 0, nt, ots, &g_status);
+    } else if (peak)  // cropped maps: the row-pair form
+        emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, zf::C2rPairCfg<W2>::SMEM,
+                   zf::k_row_c2r_pair<W2, zf::kStorePeak>, map, out, peak, tw, orows, ocols, ocols,
+                   nt, ots, &g_status);
     else
-        emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_row_c2r<W2, zf::kStoreMap>,
-                   map, out, (int*)nullptr, nf, nf, np, tw, orows, ocols, ocols, 0, 0, nt, ots,
-                   &g_status);
+        emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, zf::C2rPairCfg<W2>::SMEM,
+                   zf::k_row_c2r_pair<W2, zf::kStoreMap>, map, out, np, tw, orows, ocols, ocols, nt,
+                   ots, &g_status);
 }
 
 #define EMU_SIZES(X) X(64) X(128) X(256) X(512) X(2048) X(120) X(240)
@@ -413,7 +424,8 @@ int main(int argc, char** argv) {
     const bool max_mode = hd[12] == 1 || hd[12] == 2;  // fold into running max / argmax maps
     const bool stats = hd[12] == 2;                    // ... and into sum / sum-of-squares maps
     const bool peaks_mode = hd[12] == 3;               // maps plus per-template peaks
-    const int group = max_mode ? 0 : hd[13];           // >= 2: batched groups
+    const int group = max_mode ? 0 : (hd[13] & 0xFFFF);  // >= 2: batched groups
+    const bool poison = (hd[13] >> 16) & 1;              // workspace starts as NaN
     const int W2 = W / 2;
     std::vector<float> tm((size_t)B * sy * sx);
     std::vector<float2> spec((size_t)(W2 + 1) * H);
@@ -430,6 +442,8 @@ int main(int argc, char** argv) {
                                           : q_elems + (chunk > 0 ? chunk : 0) * r_elems;
     std::vector<float4> ws_store((ws_elems + 1) / 2 + 1);
     float2* Q = reinterpret_cast<float2*>(ws_store.data());
+    if (poison)
+        for (auto& v4 : ws_store) v4 = float4{NAN, NAN, NAN, NAN};
     float2* Rregion = Q + q_elems;
     std::vector<float> out((size_t)(max_mode ? 1 : B) * oy * ox);
     std::vector<int> arg(max_mode ? (size_t)oy * ox : 0);

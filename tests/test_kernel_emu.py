@@ -47,7 +47,7 @@ def nz_of(n, length):
 
 
 def run_emu(exe, tmp_path, B, sy, sx, H, W, conj, full, nz_col=None, nz_row=None, seed=0,
-            chunk=0, max_mode=False, group=0):
+            chunk=0, max_mode=False, group=0, poison=False):
     rng = np.random.default_rng(seed)
     img = rng.standard_normal((H, W)).astype(np.float32)
     tm = rng.standard_normal((B, sy, sx)).astype(np.float32)
@@ -58,7 +58,7 @@ def run_emu(exe, tmp_path, B, sy, sx, H, W, conj, full, nz_col=None, nz_row=None
     fin, fout = str(tmp_path / "in.bin"), str(tmp_path / "out.bin")
     with open(fin, "wb") as f:
         np.array([B, sy, sx, H, W, oy, ox, int(conj), 3, nz_col, nz_row, chunk, int(max_mode),
-                  group], np.int32).tofile(f)
+                  group + (1 << 16 if poison else 0)], np.int32).tofile(f)
         tm.tofile(f)
         spec.tofile(f)
     res = subprocess.run([exe, fin, fout], capture_output=True, text=True)
@@ -218,3 +218,16 @@ def test_emulated_batched_peaks(emu, tmp_path):
     (out, peaks), ref = run_emu(emu, tmp_path, B, 12, 10, H, W, True, False, max_mode=3, group=2)
     assert O.rel_l2(ref, out) < 1e-6
     assert np.array_equal(peaks, out.reshape(B, -1).max(axis=1))
+
+
+def test_emulated_pair_kernel_ignores_stale_rows(emu, tmp_path):
+    """Odd valid-crop height: the row pair's second row lies past the output
+    and was never written by the column pass; a NaN-poisoned workspace must
+    not leak into the last output row (the harness fills the workspace with
+    NaN in this mode)."""
+    # out 81 x 224: odd height, and row 81 lies past the template's rows (48),
+    # so nothing ever wrote it
+    B, sy, sx, H, W = 2, 48, 33, 128, 256
+    out, ref = run_emu(emu, tmp_path, B, sy, sx, H, W, True, False, group=0, poison=True)
+    assert np.all(np.isfinite(out))
+    assert O.rel_l2(ref, out) < 1e-6

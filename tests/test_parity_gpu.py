@@ -304,3 +304,19 @@ def test_batched_groups_agree_with_per_template_path(B, sy, sx, H, W, full, conj
         torch.cuda.synchronize()
         assert np.array_equal(out.cpu().numpy(), b)
         assert torch.equal(peaks, out.reshape(B, -1).amax(dim=1))
+
+
+@pytest.mark.parametrize("H,W,sy,sx", [(512, 256, 48, 33), (4096, 4096, 256, 256)])
+def test_valid_crop_with_nan_workspace(H, W, sy, sx):
+    """A workspace that starts as NaN (nothing in it needs initialising):
+    with an odd valid-crop height the inverse row pass pairs the last output
+    row with a row the column pass never wrote, which must not leak in."""
+    _, tm, spec = make_inputs(2, sy, sx, H, W, seed=H + sy)
+    dev = torch.device("cuda", 0)
+    for ws in (torch.full((2, H, W // 2 + 1), complex(float("nan"), float("nan")),
+                          dtype=torch.complex64, device=dev),
+               torch.full((H * (W // 2),), complex(float("nan"), float("nan")),
+                          dtype=torch.complex64, device=dev)):
+        out = capi_corr(tm, spec, H, W, False, True, ws=ws)
+        ref = O.padded_corr2d_f64(tm.numpy(), spec.numpy(), H, W, True, False)
+        assert_parity(ref, out, what=f"NaN workspace {tuple(ws.shape)}")

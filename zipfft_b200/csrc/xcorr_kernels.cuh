@@ -896,4 +896,170 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     }
 }
 
+// ===========================================================================
+// Kernel 3, row-pair form (the map epilogues).  The two real rows y0, y1 of a
+// pair come out of ONE W-point complex inverse FFT of Z = X_y0 + i X_y1, both
+// spectra extended by Hermitian symmetry (X[W - k] = conj X[k]) from the
+// packed tile: out[y0] = Re z, out[y1] = Im z.  This replaces the split
+// pre-pass of the W/2-point form (one 16-byte read and two adds per element
+// instead of two reads and two complex products).  Same tiles, tensor map and
+// block size as k_row_c2r: a pair's W-point transform has twice the threads
+// of a row's W/2-point one.
+// ===========================================================================
+template <int W2>
+struct C2rPairCfg {
+    using C = C2rCfg<W2>;
+    static constexpr int W = 2 * W2;
+    static constexpr int TP = fft_threads(W);  // threads per pair
+    static constexpr int PPB = C::RPB / 2;     // pairs per block
+    static constexpr int XB = xbuf_len(W);
+    static constexpr int FLOATS = 2 * C::QB + PPB * XB;
+    static constexpr int SMEM = FLOATS * 8 + 2 * 8;
+    static_assert(PPB * TP == C::THREADS, "a pair's transform has twice a row's threads");
+};
+
+template <int W2, int MODE>
+__global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
+    k_row_c2r_pair(const __grid_constant__ CUtensorMap qmap, float* __restrict__ out,
+                   unsigned* __restrict__ peak, const float2* __restrict__ twW, int out_rows,
+                   int out_cols, int out_pitch, int ntemplates, long long out_tstride,
+                   int* __restrict__ status) {
+    static_assert(MODE == kStoreMap || MODE == kStorePeak, "map epilogues only");
+    using C = C2rCfg<W2>;
+    using P = C2rPairCfg<W2>;
+    constexpr int W = P::W, TP = P::TP;
+    using I = Stockham<W, TP, true, false>;
+    static_assert(I::S >= 2, "row FFT needs at least two stages");
+    constexpr int R0 = I::radix(0), NB0 = I::nbf(0);
+    constexpr int RL = I::radix(I::S - 1), NBL = I::nbf(I::S - 1);
+
+    const int tid = threadIdx.x;
+    const int pr = tid / TP, t = tid % TP;
+    float2* smem = dyn_smem();
+    float2* qbase = smem;  // [2][W2][RPB]
+    float2* xbuf = smem + 2 * C::QB + pr * P::XB;
+    uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + P::FLOATS);
+
+    if (tid == 0) {
+        mbar_init(&mbar[0], 1);
+        mbar_init(&mbar[1], 1);
+        mbar_init_fence();
+    }
+    __syncthreads();
+
+    pdl_launch_dependents();
+    typename I::Twiddles tw;
+    I::template load_twiddles<W>(tw, twW, t);
+    // Q comes from the previous kernel.
+    pdl_wait_prerequisites();
+
+    // Units (template, row group) as in k_row_c2r.
+    const int ngroups = (out_rows + C::RPB - 1) / C::RPB;
+    const int units = ngroups * ntemplates;
+    const uint64_t pol_keep = l2_evict_last();
+    const uint64_t pol_stream = l2_evict_first();
+    auto issue = [&](int b, int u) {
+        const int tj = u / ngroups, grp = u - tj * ngroups;
+        mbar_arrive_expect_tx(&mbar[b], (uint32_t)(W2 * C::RPB * 8));
+        for (int k0 = 0; k0 < W2; k0 += C::BOXK)
+            tma_load_2d(qbase + b * C::QB + k0 * C::RPB, &qmap, grp * C::RPB, tj * W2 + k0,
+                        &mbar[b], pol_keep);
+    };
+
+    int u = blockIdx.x;
+    if (tid == 0 && u < units) issue(0, u);
+    for (int it = 0; u < units; ++it, u += gridDim.x) {
+        const int tj = u / ngroups, grp = u - tj * ngroups;
+        float* outj = out + tj * out_tstride;
+        const int b = it & 1;
+        const uint32_t parity = (it >> 1) & 1;
+        const bool more = u + (int)gridDim.x < units;
+        if (tid == 0 && more) issue(b ^ 1, u + gridDim.x);
+        const bool ok = mbar_wait_bounded(&mbar[b], parity);
+        if (__syncthreads_or(!ok)) {
+            if (tid == 0) {
+                atomicExch(status, kStatusTimeout);
+                if (more) mbar_wait_bounded(&mbar[b ^ 1], ((it + 1) >> 1) & 1);
+            }
+            return;
+        }
+
+        // Stage-0 inputs Z[k], k = bb + r NB0: for k <= W2 from column k of the
+        // tile, above from column W - k (conjugated); both rows of the pair in
+        // one 16-byte read (X0.x, X0.y, X1.x, X1.y).  Packed column 0 holds
+        // X[0] (real part) and X[W2] (imaginary part).  A second row past the
+        // output (odd out_rows) was never written by the column pass: it
+        // enters as zero, so that its stale contents cannot leak into the
+        // first row through rounding (or as NaN).
+        const int y0 = grp * C::RPB + 2 * pr;
+        const bool has0 = y0 < out_rows, has1 = y0 + 1 < out_rows;
+        const float2* qt = qbase + b * C::QB + 2 * pr;
+        float2 v[I::MAXE];
+#pragma unroll
+        for (int q = 0; q < I::bpt(0); ++q) {
+            const int bb = t + q * TP;
+            if (I::even(0) || bb < NB0) {
+#pragma unroll
+                for (int r = 0; r < R0; ++r) {
+                    const int k = bb + r * NB0;
+                    const bool hi = k > W2;
+                    const int j = hi ? W - k : k;
+                    const int jt = j == W2 ? 0 : j;
+                    float4 x = *reinterpret_cast<const float4*>(qt + jt * C::RPB);
+                    if (!has1) x.z = x.w = 0.f;
+                    float2 z;
+                    if (j == 0)
+                        z = c_make(x.x, x.z);
+                    else if (j == W2)
+                        z = c_make(x.y, x.w);
+                    else if (!hi)
+                        z = c_make(x.x - x.w, x.y + x.z);  // X0 + i X1
+                    else
+                        z = c_make(x.x + x.w, x.z - x.y);  // conj X0 + i conj X1
+                    v[q * R0 + r] = z;
+                }
+            }
+        }
+        I::run_regs(v, xbuf, tw, t);
+
+        // z[n] = out[y0][n] + i out[y1][n], n = bb + r NBL.
+        float* row0 = outj + (size_t)y0 * out_pitch;
+        float* row1 = row0 + out_pitch;
+        float pk = -INFINITY;
+        auto emit = [&](auto full_width) {
+            constexpr bool FULL = decltype(full_width)::value;
+#pragma unroll
+            for (int q = 0; q < I::bpt(I::S - 1); ++q) {
+                const int bb = t + q * TP;
+                if (I::even(I::S - 1) || bb < NBL) {
+#pragma unroll
+                    for (int r = 0; r < RL; ++r) {
+                        const int n = bb + r * NBL;
+                        const float2 z = v[q * RL + r];
+                        if (FULL || n < out_cols) {
+                            if (has0) {
+                                st_hint(row0 + n, z.x, pol_stream);
+                                if constexpr (MODE == kStorePeak) pk = fmaxf(pk, z.x);
+                            }
+                            if (has1) {
+                                st_hint(row1 + n, z.y, pol_stream);
+                                if constexpr (MODE == kStorePeak) pk = fmaxf(pk, z.y);
+                            }
+                        }
+                    }
+                }
+            }
+        };
+        if (out_cols == W)
+            emit(std::true_type{});
+        else
+            emit(std::false_type{});
+        if constexpr (MODE == kStorePeak) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) pk = fmaxf(pk, __shfl_xor_sync(0xffffffffu, pk, o));
+            if ((tid & 31) == 0) atomicMax(peak + tj, ordered_key(pk));
+        }
+    }
+}
+
 }  // namespace zf
