@@ -672,8 +672,26 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     // Output rows leave through per-thread stores: staging them for bulk
     // stores needs one more block barrier per group, which cost more than the
     // store-queue stalls it removed.
+    // Running-map modes: L2 prefetch of the rows of the maps that unit u's
+    // epilogue reads (one template per launch in these modes).
+    auto prefetch_maps = [&](int uu) {
+        const int g0 = (uu - (uu / ngroups) * ngroups) * C::RPB;
+        for (int r = 0; r < C::RPB; ++r) {
+            const int yy = g0 + r;
+            if (yy >= out_rows) break;
+            prefetch_row(out + (size_t)yy * out_pitch, out_cols);
+            if constexpr (MODE == kRunningStats) {
+                prefetch_row(sum + (size_t)yy * out_pitch, out_cols);
+                prefetch_row(sumsq + (size_t)yy * out_pitch, out_cols);
+            }
+        }
+    };
+
     int u = blockIdx.x;
     if (tid == 0 && u < units) issue(0, u);
+    if constexpr (MODE == kRunningMax || MODE == kRunningStats) {
+        if (tid == 0 && u < units) prefetch_maps(u);
+    }
     for (int it = 0; u < units; ++it, u += gridDim.x) {
         const int tj = u / ngroups, grp = u - tj * ngroups;
         float* outj = out + tj * out_tstride;
@@ -681,20 +699,11 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
         const uint32_t parity = (it >> 1) & 1;
         const bool more = u + (int)gridDim.x < units;
         if (tid == 0 && more) issue(b ^ 1, u + gridDim.x);
-        if constexpr (MODE != kStoreMap) {
-            // The maps this group's epilogue reads: into L2 while the group
-            // is transformed (whole 16-byte chunks inside each row only).
-            if (tid == 0) {
-                for (int r = 0; r < C::RPB; ++r) {
-                    const int yy = grp * C::RPB + r;
-                    if (yy >= out_rows) break;
-                    prefetch_row(outj + (size_t)yy * out_pitch, out_cols);
-                    if constexpr (MODE == kRunningStats) {
-                        prefetch_row(sum + (size_t)yy * out_pitch, out_cols);
-                        prefetch_row(sumsq + (size_t)yy * out_pitch, out_cols);
-                    }
-                }
-            }
+        if constexpr (MODE == kRunningMax || MODE == kRunningStats) {
+            // The maps the NEXT group's epilogue reads: into L2 a whole
+            // iteration ahead (whole 16-byte chunks inside each row only).
+            // The first group's were requested before the loop.
+            if (tid == 0 && more) prefetch_maps(u + gridDim.x);
         }
         const bool ok = mbar_wait_bounded(&mbar[b], parity);
         if (__syncthreads_or(!ok)) {
