@@ -280,6 +280,12 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
         }
     };
 
+    // Double buffering: thread 0 refills the other pair of buffers with the
+    // next group once the block is past this group's barrier (their last
+    // readers are behind it) and the previous column's bulk store, staged in
+    // the other spectrum buffer, has read it; the block never waits for that
+    // store.  (Refilling before the wait, or filling both buffers up front,
+    // measured slower.)
     int u = blockIdx.x;
     if (tid == 0 && u < units) issue(0, u);
     for (int it = 0; u < units; ++it, u += gridDim.x) {
@@ -288,20 +294,18 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
         const int tj = u / cgroups, vc0 = (u - tj * cgroups) * C::FPB;
         float2* Qj = Q + tj * q_tstride;
         const float2* Rj = R + tj * r_tstride;
-        // The other buffer was last read before this iteration's barriers.
         const bool more = u + (int)gridDim.x < units;
-        if (tid == 0 && more) issue(b ^ 1, u + gridDim.x);
         const bool ok = mbar_wait_bounded(&mbar[b], parity);
-        // The previous column's bulk store must have read the exchange buffer
-        // before this column writes it (the barrier below publishes that).
-        if (tid == 0) bulk_wait_read();
         if (__syncthreads_or(!ok)) {
             if (tid == 0) {
                 atomicExch(status, kStatusTimeout);
-                if (more) mbar_wait_bounded(&mbar[b ^ 1], ((it + 1) >> 1) & 1);
                 bulk_wait_all();
             }
             return;
+        }
+        if (tid == 0 && more) {
+            bulk_wait_read();
+            issue(b ^ 1, u + gridDim.x);
         }
 
         const int vc = vc0 + g;
@@ -370,22 +374,24 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
 
         if constexpr (C::FPB == 1) {
             if (mode == 0) {  // block-uniform (one column per block)
-                // Stage the column in the exchange buffer (its last reader
-                // finished before the transform's final barrier) and store it
-                // with one bulk copy.
+                // Stage the column in this group's spectrum buffer (read only
+                // by the product, before the inverse transform's barriers) and
+                // store it with one bulk copy; the exchange buffer is then free
+                // for the next column at once.
+                float2* stage = sbase + b * C::FPB * C::SB;
 #pragma unroll
                 for (int q = 0; q < I::bpt(I::S - 1); ++q) {
                     const int bb = t + q * C::T;
                     if (I::even(I::S - 1) || bb < NBO) {
 #pragma unroll
-                        for (int r = 0; r < RO; ++r) xbuf[bb + r * NBO] = v[q * RO + r];
+                        for (int r = 0; r < RO; ++r) stage[bb + r * NBO] = v[q * RO + r];
                     }
                 }
                 fence_proxy_async();
                 __syncthreads();
                 if (tid == 0) {
                     const int rows = store_rows >= H ? H : ((store_rows + 1) & ~1);
-                    tma_store_1d(Qj + (size_t)vc * H, xbuf, (uint32_t)rows * 8u, pol_keep);
+                    tma_store_1d(Qj + (size_t)vc * H, stage, (uint32_t)rows * 8u, pol_keep);
                     bulk_commit();
                 }
                 continue;
