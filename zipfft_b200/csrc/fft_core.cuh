@@ -536,23 +536,25 @@ struct Stockham {
     // Stages s .. S-1 where stage s-1's outputs are in registers.  Ends with
     // the last stage's outputs in registers: v[q R + r] = X[b + r N/R].
     // Every thread of the block must call this (it synchronises the block).
-    template <int s, class TWS>
+    // TAIL = false leaves out the barrier after the last stage's loads; the
+    // caller then passes a block barrier of its own before writing buf again.
+    template <int s, bool TAIL = true, class TWS>
     ZF_DEV static void run_from(float2 (&v)[MAXE], float2* buf, const TWS& tw, int t) {
         if constexpr (s < S) {
             store<s - 1>(v, buf, t);
             __syncthreads();
             load<s>(v, buf, t);
-            __syncthreads();
+            if constexpr (TAIL || s + 1 < S) __syncthreads();
             compute<s>(v, tw);
-            run_from<s + 1>(v, buf, tw, t);
+            run_from<s + 1, TAIL>(v, buf, tw, t);
         }
     }
 
     // Full transform whose stage-0 input is in registers (layout of stage 0).
-    template <class TWS>
+    template <bool TAIL = true, class TWS>
     ZF_DEV static void run_regs(float2 (&v)[MAXE], float2* buf, const TWS& tw, int t) {
         compute<0>(v, tw);
-        run_from<1>(v, buf, tw, t);
+        run_from<1, TAIL>(v, buf, tw, t);
     }
 
     // Full transform whose input is in the shared buffer (natural order,

@@ -366,10 +366,13 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
             }
         }
 
+        // No barrier after the inverse's last exchange: the next write of the
+        // exchange buffer is the next group's transform, behind the loop-top
+        // barrier (the staged column goes to the spectrum buffer).
         if constexpr (kShare) {
-            I::run_regs(v, xbuf, twf, t);
+            I::template run_regs<false>(v, xbuf, twf, t);
         } else {
-            I::run_regs(v, xbuf, twi_own, t);
+            I::template run_regs<false>(v, xbuf, twi_own, t);
         }
 
         if constexpr (C::FPB == 1) {
