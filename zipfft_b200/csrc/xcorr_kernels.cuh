@@ -746,7 +746,10 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                 });
             }
         }
-        I::run_regs(v, xbuf, tw, t);
+        // No barrier after the last exchange: the epilogue uses registers and
+        // global memory only, and the next group's first write of the
+        // exchange buffer is behind the loop-top barrier.
+        I::template run_regs<false>(v, xbuf, tw, t);
 
         const int y = grp * C::RPB + g;
         float pk = -INFINITY;  // kStorePeak: this thread's largest stored value
@@ -1038,7 +1041,10 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                 }
             }
         }
-        I::run_regs(v, xbuf, tw, t);
+        // No barrier after the last exchange: the epilogue uses registers and
+        // global memory only, and the next group's first write of the
+        // exchange buffer is behind the loop-top barrier.
+        I::template run_regs<false>(v, xbuf, tw, t);
 
         // z[n] = out[y0][n] + i out[y1][n], n = bb + r NBL.
         float* row0 = outj + (size_t)y0 * out_pitch;
