@@ -4,8 +4,10 @@
 // array and a std::barrier for __syncthreads; blocks run one after another.
 // Built with AddressSanitizer, this checks the kernels' index arithmetic
 // (every global and shared access in bounds) and their arithmetic against the
-// oracle on small sizes before any of it runs on a GPU.  It is never part of
-// the library: the library has no CPU path.
+// oracle on small sizes before any of it runs on a GPU; it also checks that
+// no barrier is divergent within a warp and that no bulk store's shared-memory
+// source is written before the store's read is waited for.  It is never part
+// of the library: the library has no CPU path.
 //
 // Usage: zf_emu <in.bin> <out.bin>, or zf_emu spectrum <in.bin> <out.bin>
 //   in.bin : int32 header {B, sy, sx, H, W, oy, ox, conj, grid_cap, nz_col,
@@ -198,6 +200,33 @@ void zf::emu_check_store(const void* dst, const void* src, uint32_t bytes) {
         std::abort();
     }
 }
+// Bulk stores in flight, per issuing thread: the source bytes as they were at
+// issue.  The GPU may read the source at any time until the issuing thread's
+// wait_group.read, so a write to it before that wait (by any thread, or by a
+// TMA load refilling the buffer) races with the store; the wait checks that
+// the source still holds the recorded bytes.  A block must wait for all its
+// stores before it exits (checked after each block).
+struct EmuPendingStore {
+    const unsigned char* src;
+    std::vector<unsigned char> bytes;
+};
+thread_local std::vector<EmuPendingStore> emu_pending_stores;
+void zf::emu_store_issued(const void* src, uint32_t bytes) {
+    const auto* s = static_cast<const unsigned char*>(src);
+    emu_pending_stores.push_back({s, std::vector<unsigned char>(s, s + bytes)});
+}
+void zf::emu_store_wait_read() {
+    for (const auto& p : emu_pending_stores) {
+        if (std::memcmp(p.src, p.bytes.data(), p.bytes.size()) != 0) {
+            std::fprintf(stderr, "bulk store source %p overwritten before the store's read "
+                                 "was waited for (thread %u, block %u)\n",
+                         static_cast<const void*>(p.src), threadIdx.x, blockIdx.x);
+            std::abort();
+        }
+    }
+    emu_pending_stores.clear();
+}
+
 // TMA rules: 16-byte aligned addresses and sizes, destination inside the
 // block's shared memory.
 void zf::emu_check_copy(const void* dst, const void* src, uint32_t bytes) {
@@ -240,6 +269,12 @@ void emu_launch(dim3 grid, int block, size_t smem_bytes, K kernel, A... args) {
                     blockIdx.x = bx;
                     blockIdx.y = by;
                     kernel(args...);
+                    if (!emu_pending_stores.empty()) {
+                        std::fprintf(stderr, "block %u exited with %zu bulk store(s) not waited "
+                                             "for (thread %d)\n",
+                                     bx, emu_pending_stores.size(), tid);
+                        std::abort();
+                    }
                     bar.arrive_and_wait();
                 }
             }

@@ -190,15 +190,21 @@ inline void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* ba
     emu_mbar_complete_tx(bar, bytes);
 }
 void emu_check_store(const void* dst, const void* src, uint32_t bytes);
+// A bulk store may read its shared-memory source at any time up to the
+// issuing thread's wait: the harness records the source at issue and checks
+// at the wait that nothing has written it since.
+void emu_store_issued(const void* src, uint32_t bytes);
+void emu_store_wait_read();
 inline void tma_store_1d(void* dst, const void* src, uint32_t bytes, uint64_t) {
     emu_check_store(dst, src, bytes);
     std::memcpy(dst, src, bytes);
+    emu_store_issued(src, bytes);
 }
 inline void pdl_launch_dependents() {}
 inline void pdl_wait_prerequisites() {}
 inline void bulk_commit() {}
-inline void bulk_wait_read() {}
-inline void bulk_wait_all() {}
+inline void bulk_wait_read() { emu_store_wait_read(); }
+inline void bulk_wait_all() { emu_store_wait_read(); }
 inline void fence_proxy_async() {}
 inline void st_hint(float2* p, float2 v, uint64_t) { *p = v; }
 inline void st_hint(float* p, float v, uint64_t) { *p = v; }
