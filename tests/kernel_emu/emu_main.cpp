@@ -5,14 +5,16 @@
 // Built with AddressSanitizer, this checks the kernels' index arithmetic
 // (every global and shared access in bounds) and their arithmetic against the
 // oracle on small sizes before any of it runs on a GPU; it also checks that
-// no barrier is divergent within a warp and that no bulk store's shared-memory
-// source is written before the store's read is waited for.  It is never part
-// of the library: the library has no CPU path.
+// no barrier is divergent within a warp, that no bulk store's shared-memory
+// source is written before the store's read is waited for, and (in the
+// deferred-arrival mode) that no TMA-loaded buffer is read before its barrier
+// wait.  It is never part of the library: the library has no CPU path.
 //
 // Usage: zf_emu <in.bin> <out.bin>, or zf_emu spectrum <in.bin> <out.bin>
 //   in.bin : int32 header {B, sy, sx, H, W, oy, ox, conj, grid_cap, nz_col,
 //            nz_row, chunk, max_mode, group (+ 1 << 16: workspace filled with
-//            NaN first)}, float32 templates [B][sy][sx],
+//            NaN first; + 1 << 17: TMA loads delivered only when a thread
+//            polls their barrier)}, float32 templates [B][sy][sx],
 //            complex64 spectrum [W/2+1][H]
 //   out.bin: float32 [B][oy][ox] maps, or with max_mode the float32 [oy][ox]
 //            running maximum and int32 [oy][ox] argmax over the templates,
@@ -167,9 +169,47 @@ void zf::emu_mbar_complete_tx(uint64_t* bar, uint32_t bytes) {
     b.tx -= bytes;
     emu_bar_complete(b);
 }
+// TMA loads: delivered at issue (a refill that lands while the buffer is
+// still being read then corrupts the results), or with emu_defer_loads only
+// when a thread next polls the load's barrier (a read of a buffer before its
+// barrier wait then sees the old contents).  In deferred mode a block must
+// not exit with a load still undelivered.
+static bool emu_defer_loads = false;
+struct EmuPendingLoad {
+    uint64_t* bar;
+    void* dst;
+    std::vector<unsigned char> bytes;
+};
+static std::vector<EmuPendingLoad> emu_pending_loads;  // guarded by emu_bar_mu
+void zf::emu_tma_arrive(void* dst, const void* data, uint32_t bytes, uint64_t* bar) {
+    if (!emu_defer_loads) {
+        std::memcpy(dst, data, bytes);
+        emu_mbar_complete_tx(bar, bytes);
+        return;
+    }
+    const auto* d = static_cast<const unsigned char*>(data);
+    std::lock_guard<std::mutex> l(emu_bar_mu);
+    emu_pending_loads.push_back({bar, dst, std::vector<unsigned char>(d, d + bytes)});
+}
 bool zf::emu_mbar_try_wait(uint64_t* bar, uint32_t parity) {
     std::lock_guard<std::mutex> l(emu_bar_mu);
-    return emu_bars.at(bar).phase != parity;  // the phase with that parity completed
+    EmuBar& b = emu_bars.at(bar);
+    for (size_t i = 0; i < emu_pending_loads.size();) {
+        EmuPendingLoad& p = emu_pending_loads[i];
+        if (p.bar != bar) {
+            ++i;
+            continue;
+        }
+        std::memcpy(p.dst, p.bytes.data(), p.bytes.size());
+        b.tx -= (long long)p.bytes.size();
+        emu_bar_complete(b);
+        emu_pending_loads.erase(emu_pending_loads.begin() + (long)i);
+    }
+    return b.phase != parity;  // the phase with that parity completed
+}
+static size_t emu_pending_load_count() {
+    std::lock_guard<std::mutex> l(emu_bar_mu);
+    return emu_pending_loads.size();
 }
 // Bulk L2 prefetch rule: 16-byte aligned address and size; the emulator
 // also reads the range, so ASan flags a prefetch outside any allocation.
@@ -276,6 +316,12 @@ void emu_launch(dim3 grid, int block, size_t smem_bytes, K kernel, A... args) {
                         std::abort();
                     }
                     bar.arrive_and_wait();
+                    if (tid == 0 && emu_pending_load_count() != 0) {
+                        std::fprintf(stderr, "block %u exited with %zu TMA load(s) in flight\n",
+                                     bx, emu_pending_load_count());
+                        std::abort();
+                    }
+                    bar.arrive_and_wait();  // the check precedes the next block's loads
                 }
             }
         });
@@ -461,6 +507,7 @@ int main(int argc, char** argv) {
     const bool peaks_mode = hd[12] == 3;               // maps plus per-template peaks
     const int group = max_mode ? 0 : (hd[13] & 0xFFFF);  // >= 2: batched groups
     const bool poison = (hd[13] >> 16) & 1;              // workspace starts as NaN
+    emu_defer_loads = (hd[13] >> 17) & 1;                // TMA loads land at the wait
     const int W2 = W / 2;
     std::vector<float> tm((size_t)B * sy * sx);
     std::vector<float2> spec((size_t)(W2 + 1) * H);

@@ -47,7 +47,7 @@ def nz_of(n, length):
 
 
 def run_emu(exe, tmp_path, B, sy, sx, H, W, conj, full, nz_col=None, nz_row=None, seed=0,
-            chunk=0, max_mode=False, group=0, poison=False):
+            chunk=0, max_mode=False, group=0, poison=False, defer=False):
     rng = np.random.default_rng(seed)
     img = rng.standard_normal((H, W)).astype(np.float32)
     tm = rng.standard_normal((B, sy, sx)).astype(np.float32)
@@ -58,7 +58,8 @@ def run_emu(exe, tmp_path, B, sy, sx, H, W, conj, full, nz_col=None, nz_row=None
     fin, fout = str(tmp_path / "in.bin"), str(tmp_path / "out.bin")
     with open(fin, "wb") as f:
         np.array([B, sy, sx, H, W, oy, ox, int(conj), 3, nz_col, nz_row, chunk, int(max_mode),
-                  group + (1 << 16 if poison else 0)], np.int32).tofile(f)
+                  group + (1 << 16 if poison else 0) + (1 << 17 if defer else 0)],
+                 np.int32).tofile(f)
         tm.tofile(f)
         spec.tofile(f)
     res = subprocess.run([exe, fin, fout], capture_output=True, text=True)
@@ -231,3 +232,40 @@ def test_emulated_pair_kernel_ignores_stale_rows(emu, tmp_path):
     out, ref = run_emu(emu, tmp_path, B, sy, sx, H, W, True, False, group=0, poison=True)
     assert np.all(np.isfinite(out))
     assert O.rel_l2(ref, out) < 1e-6
+
+
+@pytest.mark.parametrize("case", [
+    # B, sy, sx, H, W, conj, full, chunk, max_mode, group
+    (2, 100, 20, 2048, 64, True, True, 2, 0, 0),    # one column per block, bulk Q stores
+    (1, 129, 9, 2048, 64, False, False, 0, 0, 0),   # valid crop: row-pair kernel
+    (5, 16, 16, 64, 64, True, True, 2, 0, 0),       # several columns per block, chunked rows
+    (2, 10, 100, 64, 2048, True, True, 2, 0, 0),    # wide rows
+    (4, 9, 13, 120, 240, True, False, 0, 0, 4),     # batched group
+    (3, 12, 9, 128, 128, True, True, 0, 1, 0),      # running max / argmax
+    (3, 12, 9, 128, 128, True, False, 0, 2, 0),     # ... with sum / sum of squares
+    (3, 12, 10, 64, 256, True, False, 0, 3, 0),     # per-template peaks
+], ids=lambda c: str(c))
+def test_emulated_kernels_with_late_tma_arrival(emu, tmp_path, case):
+    """Every TMA load lands only when a thread polls its barrier, the latest
+    moment the hardware allows: a read of a double-buffered input before its
+    barrier wait would see the previous group's data.  Results must not
+    change, and no block may exit with a load in flight."""
+    B, sy, sx, H, W, conj, full, chunk, max_mode, group = case
+    got, ref = run_emu(emu, tmp_path, B, sy, sx, H, W, conj, full, chunk=chunk,
+                       max_mode=max_mode, group=group, defer=True)
+    if max_mode in (1, 2):
+        mx, am = got[0], got[1]
+        peak = np.abs(ref).max()
+        assert np.allclose(mx, ref.max(axis=0), rtol=0, atol=1e-5 * peak)
+        order = np.sort(ref, axis=0)
+        sure = order[-1] - order[-2] > 1e-4 * peak
+        assert np.array_equal(am[sure], ref.argmax(axis=0)[sure])
+        if max_mode == 2:
+            assert O.rel_l2(ref.sum(axis=0), got[2]) < 1e-5
+            assert O.rel_l2((ref ** 2).sum(axis=0), got[3]) < 1e-5
+        return
+    out = got[0] if max_mode == 3 else got
+    assert O.rel_l2(ref, out) < 1e-6
+    assert O.max_abs_over_peak(ref, out) < 1e-5
+    if max_mode == 3:
+        assert np.array_equal(got[1], out.reshape(B, -1).max(axis=1))

@@ -21,6 +21,7 @@
 #else
 #include <chrono>
 #include <cstring>
+#include <vector>
 #endif
 
 namespace zf {
@@ -181,13 +182,16 @@ inline void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
 }
 inline bool mbar_try_wait(uint64_t* bar, uint32_t parity) { return emu_mbar_try_wait(bar, parity); }
 void emu_check_copy(const void* dst, const void* src, uint32_t bytes);
+// Delivers a TMA load's bytes (read from global memory at issue) into shared
+// memory and completes them on the barrier: at once, or, in the harness's
+// deferred mode, only when a thread next polls that barrier.
+void emu_tma_arrive(void* dst, const void* data, uint32_t bytes, uint64_t* bar);
 inline uint64_t l2_evict_first() { return 1; }
 inline uint64_t l2_evict_last() { return 2; }
 inline uint64_t l2_evict_normal() { return 3; }
 inline void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t = 0) {
     emu_check_copy(dst, src, bytes);
-    std::memcpy(dst, src, bytes);
-    emu_mbar_complete_tx(bar, bytes);
+    emu_tma_arrive(dst, src, bytes, bar);
 }
 void emu_check_store(const void* dst, const void* src, uint32_t bytes);
 // A bulk store may read its shared-memory source at any time up to the
@@ -214,8 +218,9 @@ void emu_discard_line(const void* p);
 inline void l2_discard_line(const void* p) { emu_discard_line(p); }
 inline void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
                         uint64_t = 0) {
-    unsigned char* d = static_cast<unsigned char*>(dst);
     const int row = map->box0 * map->elem;
+    std::vector<unsigned char> tile((size_t)row * map->box1);
+    unsigned char* d = tile.data();
     for (int j = 0; j < map->box1; ++j) {
         const long long yy = (long long)y + j;
         for (int i = 0; i < map->box0; ++i) {
@@ -228,7 +233,7 @@ inline void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_
             }
         }
     }
-    emu_mbar_complete_tx(bar, (uint32_t)(map->box0 * map->box1 * map->elem));
+    emu_tma_arrive(dst, tile.data(), (uint32_t)tile.size(), bar);
 }
 inline long long cycle_clock() {  // nanoseconds stand in for cycles
     return (long long)std::chrono::duration_cast<std::chrono::nanoseconds>(
