@@ -21,7 +21,8 @@
 //            followed with max_mode 2 by the float32 [oy][ox] sum and sum of
 //            squares; max_mode 3: the maps followed by float32 [B] peaks
 // spectrum mode (zfft_image_spectrum's two launches):
-//   in.bin : int32 header {H, W, grid_cap}, float32 image [H][W]
+//   in.bin : int32 header {H, W, grid_cap (+ 1 << 17: TMA loads delivered
+//            only when a thread polls their barrier)}, float32 image [H][W]
 //   out.bin: complex64 [W/2+1][H]
 #include <atomic>
 #include <barrier>
@@ -468,7 +469,8 @@ static int spectrum_main(const char* in, const char* outp) {
     if (!f) return 2;
     int hd[3];
     if (std::fread(hd, sizeof(int), 3, f) != 3) return 2;
-    const int H = hd[0], W = hd[1], cap = hd[2];
+    const int H = hd[0], W = hd[1], cap = hd[2] & 0xFFFF;
+    emu_defer_loads = (hd[2] >> 17) & 1;  // TMA loads land at the wait
     std::vector<float> img((size_t)H * W);
     if (std::fread(img.data(), sizeof(float), img.size(), f) != img.size()) return 2;
     std::fclose(f);

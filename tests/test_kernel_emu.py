@@ -132,16 +132,19 @@ def test_emulated_running_max_argmax(emu, tmp_path, chunk, W, sx):
     assert np.allclose(mv, refv.max(axis=0), rtol=0, atol=1e-5 * np.abs(refv).max())
 
 
-@pytest.mark.parametrize("H,W", [(64, 64), (128, 240), (240, 120), (2048, 64), (256, 512)])
-def test_emulated_image_spectrum(emu, tmp_path, H, W):
+@pytest.mark.parametrize("H,W,defer", [(64, 64, False), (128, 240, False), (240, 120, False),
+                                       (2048, 64, False), (256, 512, False), (2048, 64, True),
+                                       (128, 240, True)])
+def test_emulated_image_spectrum(emu, tmp_path, H, W, defer):
     """zfft_image_spectrum's row and in-place column passes against the
     float64 rfft2 (transposed), including the split of packed column 0 into
-    the kx = 0 and kx = W/2 rows."""
+    the kx = 0 and kx = W/2 rows; defer: every TMA load lands only when a
+    thread polls its barrier."""
     rng = np.random.default_rng(H + W)
     img = rng.standard_normal((H, W)).astype(np.float32)
     fin, fout = str(tmp_path / "in.bin"), str(tmp_path / "out.bin")
     with open(fin, "wb") as f:
-        np.array([H, W, 3], np.int32).tofile(f)
+        np.array([H, W, 3 + (1 << 17 if defer else 0)], np.int32).tofile(f)
         img.tofile(f)
     res = subprocess.run([emu, "spectrum", fin, fout], capture_output=True, text=True)
     assert res.returncode == 0, res.stderr[-4000:]
