@@ -9,7 +9,7 @@ the per-rank maps are combined with a single all-reduce (MAX) of packed
 64-bit keys (order-preserving float bits high, inverted template index low,
 so ties keep the lowest index).  No data moves between GPUs before that one
 reduction.  The reference has no multi-GPU code; this is the search its
-README motivates (2DTM), sharded the way SURVEY's plan describes.
+README motivates (2DTM), with the template set as the sharded dimension.
 """
 from __future__ import annotations
 
