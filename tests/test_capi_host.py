@@ -119,3 +119,49 @@ def test_image_spectrum_host_validation():
     assert lib.zfft_image_spectrum(base + 2, 128, 64, (base + 15) // 16 * 16, need, 0, None) == \
         _lib.ZFFT_ERROR_INVALID_VALUE
     assert "misaligned" in _lib.last_error()
+
+
+C_CLIENT = r"""
+#include <stdio.h>
+#include <string.h>
+#include "zipfft_b200.h"
+
+int main(void) {
+    int recs[6 * 64];
+    int n = zfft_get_supported_conv_configs(recs, 64);
+    size_t ws = zfft_workspace_bytes(4096, 4096);
+    int bad = zfft_padded_real_corr_2d(NULL, 1, 16, 16, NULL, (size_t)1 << 30, NULL, NULL,
+                                       49, 49, 100, 64, 0, NULL);
+    int has_msg = strstr(zfft_get_last_error(), "Unsupported") != NULL;
+    int empty = zfft_padded_real_corr_2d(NULL, 0, 16, 16, NULL, (size_t)1 << 30, NULL, NULL,
+                                         49, 49, 64, 64, 0, NULL);
+    printf("%d %d %d %zu %d %d %d %d\n", zfft_get_version(), n,
+           zfft_is_fft_size_supported(4096), ws, bad,
+           has_msg, empty, (int)strlen(zfft_get_last_error()));
+    return 0;
+}
+"""
+
+
+def test_header_compiles_as_c_and_links(tmp_path):
+    """A plain C11 client (the path a cgo / JNI / FFI binding takes): the
+    header compiles warning-free as strict C, the program links against the
+    library and calls its host-only entry points (no GPU needed)."""
+    import shutil
+    import subprocess
+
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    lib_dir = os.path.join(ROOT, "zipfft_b200")
+    src, exe = tmp_path / "client.c", tmp_path / "client"
+    src.write_text(C_CLIENT)
+    subprocess.check_call(["gcc", "-std=c11", "-Wall", "-Wextra", "-Werror", "-pedantic",
+                           "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe),
+                           "-L", lib_dir, "-lzipfft_b200", f"-Wl,-rpath,{lib_dir}"])
+    out = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert out.returncode == 0, out.stderr
+    version, n, ok4096, ws, bad, has_msg, empty, empty_msg = map(int, out.stdout.split())
+    assert version == _lib.load().zfft_get_version()
+    assert n == 50 and ok4096 == 1 and ws == 4096 * 2048 * 8
+    assert bad == _lib.ZFFT_ERROR_UNSUPPORTED and has_msg == 1
+    assert empty == _lib.ZFFT_SUCCESS and empty_msg == 0
