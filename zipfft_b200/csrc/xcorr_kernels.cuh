@@ -609,6 +609,16 @@ constexpr int kRunningMax = 1;  // fold it into a running per-pixel max / argmax
 constexpr int kRunningStats = 2;  // ... and into per-pixel sum and sum of squares
 constexpr int kStorePeak = 3;  // write the map and fold its maximum into *peak
 
+// kStorePeak: each warp keeps its largest stored value over the row groups of
+// one template and folds it into that template's key (one atomic per warp)
+// when its block moves on to another template or ends.  An atomic per warp
+// and group put ~16k atomics on one address per 4096-row template, which
+// serialised in L2.  Every lane of the warp must call this.
+ZF_DEV void fold_warp_peak(float v, unsigned* key) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if ((threadIdx.x & 31) == 0) atomicMax(key, ordered_key(v));
+}
 
 // MODE kStoreMap: out[y][x] = correlation.  MODE kRunningMax: out is the
 // running maximum map and arg the template-index map (same pitch); where the
@@ -701,9 +711,18 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     if constexpr (MODE == kRunningMax || MODE == kRunningStats) {
         if (tid == 0 && u < units) prefetch_maps(u);
     }
+    float pk_run = -INFINITY;  // kStorePeak: this warp's template pk_t so far
+    int pk_t = -1;
     for (int it = 0; u < units; ++it, u += gridDim.x) {
         const int tj = u / ngroups, grp = u - tj * ngroups;
         float* outj = out + tj * out_tstride;
+        if constexpr (MODE == kStorePeak) {
+            if (pk_t >= 0 && pk_t != tj) {  // block-uniform
+                fold_warp_peak(pk_run, peak + pk_t);
+                pk_run = -INFINITY;
+            }
+            pk_t = tj;
+        }
         const int b = it & 1;
         const uint32_t parity = (it >> 1) & 1;
         const bool more = u + (int)gridDim.x < units;
@@ -907,13 +926,11 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                 }
             }
         }
-        if constexpr (MODE == kStorePeak) {
-            // Every lane takes part (rows past the end contribute -inf); one
-            // atomic per warp.
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) pk = fmaxf(pk, __shfl_xor_sync(0xffffffffu, pk, o));
-            if ((tid & 31) == 0) atomicMax(peak + tj, ordered_key(pk));
-        }
+        // Rows past the end contribute -inf.
+        if constexpr (MODE == kStorePeak) pk_run = fmaxf(pk_run, pk);
+    }
+    if constexpr (MODE == kStorePeak) {
+        if (pk_t >= 0) fold_warp_peak(pk_run, peak + pk_t);
     }
 }
 
@@ -989,9 +1006,18 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
 
     int u = blockIdx.x;
     if (tid == 0 && u < units) issue(0, u);
+    float pk_run = -INFINITY;  // kStorePeak: this warp's template pk_t so far
+    int pk_t = -1;
     for (int it = 0; u < units; ++it, u += gridDim.x) {
         const int tj = u / ngroups, grp = u - tj * ngroups;
         float* outj = out + tj * out_tstride;
+        if constexpr (MODE == kStorePeak) {
+            if (pk_t >= 0 && pk_t != tj) {  // block-uniform
+                fold_warp_peak(pk_run, peak + pk_t);
+                pk_run = -INFINITY;
+            }
+            pk_t = tj;
+        }
         const int b = it & 1;
         const uint32_t parity = (it >> 1) & 1;
         const bool more = u + (int)gridDim.x < units;
@@ -1078,11 +1104,10 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
             emit(std::true_type{});
         else
             emit(std::false_type{});
-        if constexpr (MODE == kStorePeak) {
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) pk = fmaxf(pk, __shfl_xor_sync(0xffffffffu, pk, o));
-            if ((tid & 31) == 0) atomicMax(peak + tj, ordered_key(pk));
-        }
+        if constexpr (MODE == kStorePeak) pk_run = fmaxf(pk_run, pk);
+    }
+    if constexpr (MODE == kStorePeak) {
+        if (pk_t >= 0) fold_warp_peak(pk_run, peak + pk_t);
     }
 }
 
