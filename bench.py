@@ -169,6 +169,38 @@ def max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
+# The clock sampler polls every 200 ms; a 20-step window of the headline
+# workload lasts ~50 ms.  The K-step window is therefore timed repeatedly,
+# back to back, until the windows add up to MIN_TIMED_MS of load, and the
+# median window is reported (each window is exactly K steps, bracketed by a
+# barrier and a device synchronisation, max over ranks).
+MIN_TIMED_MS = 2000.0
+
+
+def timed_windows(run_window, stream, world, min_total_ms=MIN_TIMED_MS, max_windows=500):
+    """Times run_window() (K steps) repeatedly until min_total_ms of device
+    time has passed; returns the list of window milliseconds, each the max
+    over ranks (so every rank takes the same number of windows)."""
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    windows: list[float] = []
+    while True:
+        torch.cuda.synchronize()
+        barrier(world)
+        ev0.record(stream)
+        run_window()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        windows.append(max_over_ranks(ev0.elapsed_time(ev1), world))
+        if sum(windows) >= min_total_ms or len(windows) >= max_windows:
+            return windows
+
+
+def window_summary(windows: list[float]) -> dict:
+    return {"count": len(windows), "ms_min": min(windows), "ms_median": statistics.median(windows),
+            "ms_max": max(windows), "reported": "median window"}
+
+
 # ---------------------------------------------------------------------------
 # CPU baseline: the reference's torch.fft path on the host cores
 # ---------------------------------------------------------------------------
@@ -283,6 +315,77 @@ def image_spectrum_timing(image, steps=20, warmup=3):
     return res
 
 
+# ---------------------------------------------------------------------------
+# The other measurement configurations (N = 1, rank 0): throughput of each
+# one through zipfft.padded_rconv2d.corr (and the search at the search
+# configuration's shapes), with the template content each one specifies.
+# ---------------------------------------------------------------------------
+def unit_variance(t: torch.Tensor) -> torch.Tensor:
+    t = t - t.mean(dim=(-2, -1), keepdim=True)
+    return (t / t.std(dim=(-2, -1), keepdim=True)).contiguous()
+
+
+def gaussian_blob_templates(n: int, size: int, sigma: float, noise_sd: float,
+                            seed: int) -> torch.Tensor:
+    """A Gaussian blob of width sigma centred in each template, plus
+    N(0, noise_sd) noise, then zero mean and unit variance."""
+    g = torch.Generator().manual_seed(seed)
+    c = (size - 1) / 2.0
+    ax = torch.arange(size, dtype=torch.float64)
+    yy, xx = torch.meshgrid(ax, ax, indexing="ij")
+    blob = torch.exp(-((yy - c) ** 2 + (xx - c) ** 2) / (2 * sigma ** 2)).float()
+    return unit_variance(blob[None] + noise_sd * torch.randn((n, size, size), generator=g))
+
+
+# (key, description, image size, template size, templates per call, content, timed calls)
+OTHER_CONFIGS = [
+    ("1", "1024^2 image N(0,1), 4 templates 128^2 N(0,1) zero-mean unit-variance, full maps",
+     1024, 128, 4, "randn", 400),
+    ("3", "4096^2 image N(0,1), 64 templates 512^2: Gaussian blob sigma 20 px + N(0, 0.1), "
+          "zero-mean unit-variance, full maps", 4096, 512, 64, "blob", 5),
+    ("4", "3840^2 image N(0,1), 128 templates 384^2 N(0,1) zero-mean unit-variance, full maps "
+          "(radix-3/5 path)", 3840, 384, 128, "randn", 4),
+]
+
+
+def measure_configs(dev) -> dict:
+    import zipfft
+    from zipfft_b200 import padded_rconv2d as P
+
+    peak, peak_src = measured_hbm_peak()
+    res = {}
+    for key, desc, n, h, b, kind, calls in OTHER_CONFIGS:
+        g = torch.Generator().manual_seed(0)
+        spec = P.image_spectrum(torch.randn((n, n), generator=g).to(dev))
+        if kind == "blob":
+            tm = gaussian_blob_templates(b, h, 20.0, 0.1, 1)
+        else:
+            tm = unit_variance(torch.randn((b, h, h), generator=torch.Generator().manual_seed(1)))
+        tm = tm.to(dev)
+        ws = torch.empty((b, n, n // 2 + 1), dtype=torch.complex64, device=dev)
+        out = torch.empty((b, n, n), dtype=torch.float32, device=dev)
+        for _ in range(3):
+            zipfft.padded_rconv2d.corr(tm, ws, spec, out, n, n)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(calls):
+            zipfft.padded_rconv2d.corr(tm, ws, spec, out, n, n)
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / calls
+        rate = b / (ms / 1e3)
+        alg = h * h * 4 + n * (n // 2 + 1) * 8 + n * n * 4
+        res[key] = {"workload": desc, "value": rate, "unit": UNIT, "ms_per_call": ms,
+                    "calls": calls, "algorithmic_bytes_per_corr": alg,
+                    "achieved_gbs": alg * rate / 1e9, "frac": alg * rate / 1e9 / peak,
+                    "peak_source": peak_src}
+        del spec, tm, ws, out
+        torch.cuda.empty_cache()
+    res["5"] = search_rate(dev, steps=2, warmup=1)
+    return res
+
+
 def run_gpu_arm(args, world, rank, local):
     import zipfft
     from zipfft_b200 import _lib
@@ -311,19 +414,21 @@ def run_gpu_arm(args, world, rank, local):
     clocks = ClockSampler(local)
     clocks.start()
     time.sleep(0.3)
-    torch.cuda.synchronize()
-    barrier(world)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    for _ in range(args.steps):
-        step()
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    barrier(world)
+    host_s = [0.0]  # host time spent inside the corr calls of the timed windows
+
+    def window():
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            step()
+        host_s[0] += time.perf_counter() - t0
+
+    windows = timed_windows(window, stream, world, min_total_ms=args.min_timed_ms)
     clk = clocks.stop()
-    ms_total = max_over_ranks(ev0.elapsed_time(ev1), world)
+    ms_total = statistics.median(windows)
     ms_step = ms_total / args.steps
     value = world * BATCH * args.steps / (ms_total / 1e3)
+    host_ms_step = 1e3 * host_s[0] / (len(windows) * args.steps)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
     # ---- per-kernel device time (separate instrumented steps) -------------
     _lib.stage_timing(True)
@@ -357,6 +462,8 @@ def run_gpu_arm(args, world, rank, local):
             tm_bufs[i].copy_(tm_host, non_blocking=True)
             ready[i].record(copy_stream)
 
+    e2e_host_s = [0.0]  # host time inside the corr calls of the timed e2e run
+
     def e2e_run(n):
         """n steps; the first copy starts after the work already on the stream."""
         for i in (0, 1):
@@ -367,23 +474,44 @@ def run_gpu_arm(args, world, rank, local):
             if s + 1 < n:
                 copy_in(b ^ 1)
             stream.wait_event(ready[b])
+            t0 = time.perf_counter()
             zipfft.padded_rconv2d.corr(tm_bufs[b], ws, spec_T, out, H, W, peaks=peaks)
+            e2e_host_s[0] += time.perf_counter() - t0
             freed[b].record(stream)
             peaks_host.copy_(peaks, non_blocking=True)
 
     e2e_run(args.warmup)
     torch.cuda.synchronize()
     barrier(world)
+    e2e_host_s[0] = 0.0
     ev0.record(stream)
     e2e_run(args.steps)
     ev1.record(stream)
     torch.cuda.synchronize()
     barrier(world)
-    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+    e2e_ms_rank = ev0.elapsed_time(ev1)
+    e2e_ms = max_over_ranks(e2e_ms_rank, world)
     e2e_value = world * BATCH * args.steps / (e2e_ms / 1e3)
 
+    # ---- per-rank figures for N > 1 (every rank's own device time) --------
+    per_rank = None
+    if world > 1:
+        import torch.distributed as dist
+
+        mine = {"rank": rank, "value": BATCH * args.steps / (ms_total / 1e3),
+                "e2e": BATCH * args.steps / (e2e_ms_rank / 1e3),
+                "host_ms_per_step_in_corr": host_ms_step,
+                "e2e_host_ms_per_step_in_corr": 1e3 * e2e_host_s[0] / args.steps}
+        gathered = [None] * world
+        dist.all_gather_object(gathered, mine)
+        per_rank = gathered
+
     # ---- comparison and baselines (rank 0, N = 1) --------------------------
-    cufft = cpu = spectrum = None
+    cufft = cpu = spectrum = configs = None
+    if rank == 0 and world == 1 and not args.skip_configs:
+        del out, ws
+        torch.cuda.empty_cache()
+        configs = measure_configs(dev)
     if rank == 0 and world == 1 and not args.skip_baselines:
         spectrum = image_spectrum_timing(image)
         rate, ms = cufft_torch_rate(spec_nat, tm)
@@ -398,7 +526,7 @@ def run_gpu_arm(args, world, rank, local):
         per_gpu = value / world
         achieved = ALG_BYTES * per_gpu / 1e9
         peak, peak_src = measured_hbm_peak()
-        traffic = measured_traffic()
+        traffic, traffic_note = measured_traffic()
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
@@ -407,7 +535,7 @@ def run_gpu_arm(args, world, rank, local):
             "config": {"workload": WORKLOAD, "image": [H, W], "template": [TH, TW],
                        "templates_per_gpu_step": BATCH, "global_batch": BATCH * world,
                        "output": "full", "parallelism": f"dp{world} (template shards)",
-                       "l2": L2_NOTE},
+                       "l2": L2_NOTE, "timing": window_summary(windows)},
             "e2e": {"value": e2e_value, "unit": UNIT,
                     "h2d_bytes_per_step": BATCH * TH * TW * 4,
                     "d2h_bytes_per_step": BATCH * 4,
@@ -419,12 +547,18 @@ def run_gpu_arm(args, world, rank, local):
             "gpu_launches": int(round(launches_per_step * args.steps)),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
+                         "traffic_source": traffic_note,
                          "unit_of_work": "one correlation (k_row_r2c + k_col_fused + k_row_c2r "
                                          "for one template)",
                          "algorithmic_bytes_per_unit": ALG_BYTES, "peak_source": peak_src},
             "kernels": kern,
             "clocks": clk,
         }
+        line["host_ms_per_step_in_corr"] = host_ms_step
+        if per_rank is not None:
+            line["per_rank"] = per_rank
+        if configs is not None:
+            line["configs"] = configs
         if cufft is not None:
             line["cufft_torch"] = cufft
         if cpu is not None:
@@ -445,13 +579,23 @@ def measured_hbm_peak():
 
 
 def measured_traffic():
-    """DRAM bytes (read + write) per correlation from the committed ncu summary."""
+    """DRAM bytes (read + write) per correlation from the committed ncu
+    summary, or None when that summary was captured on another build of the
+    library (its `build` hash differs from the current sources')."""
+    from zipfft_b200 import build as B
+
     path = os.path.join(ROOT, "profiles", "dram_traffic.json")
     try:
         with open(path) as f:
-            return float(json.load(f)["dram_bytes_per_correlation"])
+            d = json.load(f)
+        value = float(d["dram_bytes_per_correlation"])
     except (OSError, KeyError, ValueError):
-        return None
+        return None, "no ncu traffic summary"
+    cur = B.sources_hash()[:16]
+    if d.get("build") != cur:
+        return None, (f"stale: profiles/dram_traffic.json was captured on build "
+                      f"{d.get('build')}, the library is {cur}")
+    return value, f"profiles/dram_traffic.json (ncu, build {cur})"
 
 
 # ---------------------------------------------------------------------------
@@ -465,6 +609,42 @@ SEARCH_METRIC = ("2D padded cross-corr/sec folded into per-pixel max/argmax, 409
 # template + spectrum per correlation; the maps are read-modified-written per
 # template (max read, updated where improved)
 SEARCH_ALG_BYTES = SEARCH_TH * SEARCH_TH * 4 + H * (W // 2 + 1) * 8
+
+
+def search_rate(dev, steps: int, warmup: int, stats: bool = False) -> dict:
+    """One GPU: template_search over SEARCH_PER_STEP templates of 384^2 (the
+    search configuration's per-GPU share), streamed in batches of 256."""
+    from zipfft_b200 import padded_rconv2d as P
+    from zipfft_b200.search import template_search
+
+    spec = P.image_spectrum(make_image(0).to(dev))
+    g = torch.Generator().manual_seed(7)
+    tm = unit_variance(torch.randn((SEARCH_PER_STEP, SEARCH_TH, SEARCH_TH), generator=g))
+    tm = tm.pin_memory()
+
+    def step():
+        return template_search(tm, spec, H, W, batch_size=SEARCH_BATCH, full=True, stats=stats)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    rate = SEARCH_PER_STEP / (ms / 1e3)
+    peak, peak_src = measured_hbm_peak()
+    return {"workload": f"search: 4096^2 image, {SEARCH_PER_STEP} templates of {SEARCH_TH}^2 "
+                        f"N(0,1) zero-mean unit-variance per GPU, streamed from pinned host "
+                        f"memory in batches of {SEARCH_BATCH}, running max/argmax maps "
+                        f"(one GPU's share of the 8192-template search)",
+            "value": rate, "unit": UNIT, "ms_per_call": ms, "calls": steps,
+            "algorithmic_bytes_per_corr": SEARCH_ALG_BYTES,
+            "achieved_gbs": SEARCH_ALG_BYTES * rate / 1e9,
+            "frac": SEARCH_ALG_BYTES * rate / 1e9 / peak, "peak_source": peak_src}
 
 
 def run_search_arm(args, world, rank, local):
@@ -548,6 +728,12 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", choices=("zipfft", "reference"), default="zipfft")
     ap.add_argument("--skip-baselines", action="store_true",
                     help="skip the cuFFT comparison and the CPU baseline")
+    ap.add_argument("--min-timed-ms", type=float, default=MIN_TIMED_MS,
+                    help="repeat the timed K-step window until this much device time has "
+                         "passed (default 2000 ms, so that the clock sampler sees the load); "
+                         "0 times a single window (profiling captures)")
+    ap.add_argument("--skip-configs", action="store_true",
+                    help="skip the other measurement configurations (the `configs` object)")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="templates per GPU per step (default 32, the benchmarked workload; "
                          "smaller values only for profiling captures)")

@@ -144,9 +144,10 @@ ZFFT_API int zfft_padded_real_corr_2d_noalloc(const float* input, int batch, int
                                               int output_y, int output_x, int fft_size_y,
                                               int fft_size_x, int device, void* stream);
 
-/* Bytes of fft_workspace the two calls above need for an (fft_y, fft_x)
- * image: fft_y * (fft_x / 2) complex64 values, independent of the batch
- * (templates are processed one after another through the same slice).
+/* Bytes of fft_workspace that zfft_padded_real_corr_2d, _conv_2d, _corr_2d_max,
+ * _corr_2d_peaks and _corr_2d_max_stats need for an (fft_y, fft_x) image:
+ * fft_y * (fft_x / 2) complex64 values, independent of the batch (templates
+ * are processed one after another through the same slice).
  * Returns 0 for unsupported sizes.  No counterpart in the reference, which
  * sizes the workspace (batch, fft_y, fft_x/2 + 1) (binding.cu:235-245). */
 ZFFT_API size_t zfft_workspace_bytes(int fft_size_y, int fft_size_x);

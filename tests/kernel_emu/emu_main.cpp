@@ -137,6 +137,79 @@ inline T __ldg(const T* p) {
 
 float2* zf::dyn_smem() { return emu_smem; }
 
+// Named barriers (bar.sync / bar.arrive / bar.red.or with an id and a thread
+// count).  Every lane of a warp must execute the same barrier instruction
+// (they are .aligned): the lanes meet at the warp's rendezvous and compare
+// call sites and arguments first.  Each id's barrier is created per block
+// with the count of its first use, later uses must give the same count, and
+// when a block ends every id must have completed all its phases (an arrival
+// without its matching waits, as an unbalanced token hand-off would leave,
+// aborts the run).
+struct EmuNamedBar {
+    std::unique_ptr<std::barrier<>> bar;
+    unsigned count = 0;
+    std::atomic<unsigned long long> arrivals{0};
+    std::atomic<int> flag[2];
+};
+thread_local EmuNamedBar* emu_named = nullptr;  // [16], per block
+thread_local unsigned emu_named_calls[16];      // this thread's or-calls per id
+static std::mutex emu_named_mu;
+thread_local void** emu_warp_sites = nullptr;   // [32] per warp
+static void emu_warp_agree(void* site, unsigned id, unsigned count) {
+    const unsigned lane = threadIdx.x & 31u;
+    const uintptr_t key = reinterpret_cast<uintptr_t>(site) ^ (uintptr_t(id) << 48) ^ (uintptr_t(count) << 32);
+    emu_warp_sites[lane] = reinterpret_cast<void*>(key);
+    emu_warp_bar->arrive_and_wait();
+    const unsigned w0 = threadIdx.x & ~31u;
+    for (unsigned l = 0; l < 32 && w0 + l < blockDim.x; ++l) {
+        if (emu_warp_sites[l] != reinterpret_cast<void*>(key)) {
+            std::fprintf(stderr, "divergent named barrier %u in warp %u\n", id, w0 / 32);
+            std::abort();
+        }
+    }
+    emu_warp_bar->arrive_and_wait();
+}
+static EmuNamedBar& emu_named_get(unsigned id, unsigned count) {
+    if (id == 0 || id >= 16 || count == 0 || count % 32 || count > blockDim.x) {
+        std::fprintf(stderr, "bad named barrier id %u count %u\n", id, count);
+        std::abort();
+    }
+    std::lock_guard<std::mutex> l(emu_named_mu);
+    EmuNamedBar& b = emu_named[id];
+    if (!b.bar) {
+        b.bar = std::make_unique<std::barrier<>>(count);
+        b.count = count;
+    } else if (b.count != count) {
+        std::fprintf(stderr, "named barrier %u used with counts %u and %u\n", id, b.count, count);
+        std::abort();
+    }
+    return b;
+}
+__attribute__((noinline)) void zf::named_barrier_sync(uint32_t id, uint32_t count) {
+    emu_warp_agree(__builtin_return_address(0), id, count);
+    EmuNamedBar& b = emu_named_get(id, count);
+    b.arrivals.fetch_add(1);
+    b.bar->arrive_and_wait();
+}
+__attribute__((noinline)) void zf::named_barrier_arrive(uint32_t id, uint32_t count) {
+    emu_warp_agree(__builtin_return_address(0), id, count);
+    EmuNamedBar& b = emu_named_get(id, count);
+    b.arrivals.fetch_add(1);
+    (void)b.bar->arrive();
+}
+__attribute__((noinline)) bool zf::named_barrier_or(uint32_t id, uint32_t count, bool pred) {
+    emu_warp_agree(__builtin_return_address(0), id, count);
+    EmuNamedBar& b = emu_named_get(id, count);
+    const unsigned slot = emu_named_calls[id]++ & 1u;
+    if (pred) b.flag[slot].store(1);
+    b.arrivals.fetch_add(2);
+    b.bar->arrive_and_wait();
+    const bool r = b.flag[slot].load() != 0;
+    b.bar->arrive_and_wait();  // everyone has read the flag
+    b.flag[slot].store(0);
+    return r;
+}
+
 // mbarrier stand-in: phase parity, pending arrivals, transaction bytes.
 struct EmuBar {
     uint32_t phase = 0, count = 0, pending = 0;
@@ -291,6 +364,8 @@ void emu_launch(dim3 grid, int block, size_t smem_bytes, K kernel, A... args) {
     for (int w = 0; w < nwarps; ++w)
         wbars.push_back(std::make_unique<std::barrier<>>(std::min(32, block - 32 * w)));
     std::vector<float> wbuf((size_t)nwarps * 32);
+    std::vector<void*> wsites((size_t)nwarps * 32);
+    std::vector<EmuNamedBar> named(16);
     std::vector<std::thread> threads;
     for (int tid = 0; tid < block; ++tid) {
         threads.emplace_back([&, tid] {
@@ -305,10 +380,13 @@ void emu_launch(dim3 grid, int block, size_t smem_bytes, K kernel, A... args) {
             emu_sites = sites;
             emu_warp_bar = wbars[tid / 32].get();
             emu_warp_buf = wbuf.data() + (tid / 32) * 32;
+            emu_warp_sites = wsites.data() + (tid / 32) * 32;
+            emu_named = named.data();
             for (unsigned by = 0; by < grid.y; ++by) {
                 for (unsigned bx = 0; bx < grid.x; ++bx) {
                     blockIdx.x = bx;
                     blockIdx.y = by;
+                    for (auto& c : emu_named_calls) c = 0;
                     kernel(args...);
                     if (!emu_pending_stores.empty()) {
                         std::fprintf(stderr, "block %u exited with %zu bulk store(s) not waited "
@@ -321,6 +399,23 @@ void emu_launch(dim3 grid, int block, size_t smem_bytes, K kernel, A... args) {
                         std::fprintf(stderr, "block %u exited with %zu TMA load(s) in flight\n",
                                      bx, emu_pending_load_count());
                         std::abort();
+                    }
+                    if (tid == 0) {  // every named barrier ended on a completed phase
+                        for (unsigned id = 0; id < 16; ++id) {
+                            EmuNamedBar& nb = named[id];
+                            if (nb.bar && nb.arrivals.load() % nb.count != 0) {
+                                std::fprintf(stderr, "block %u ended with named barrier %u "
+                                                     "part-way through a phase (%llu arrivals, "
+                                                     "count %u)\n",
+                                             bx, id, nb.arrivals.load(), nb.count);
+                                std::abort();
+                            }
+                            // a fresh barrier for the next block
+                            nb.bar.reset();
+                            nb.count = 0;
+                            nb.arrivals = 0;
+                            nb.flag[0] = nb.flag[1] = 0;
+                        }
                     }
                     bar.arrive_and_wait();  // the check precedes the next block's loads
                 }
@@ -341,14 +436,33 @@ static std::vector<float2> twiddles(int n) {
 
 static int g_status = 0;
 
+// Per-thread twiddle tables (Stockham::fill_thread_twiddles), built on the
+// host from the same root table the kernels' loads would read, as the
+// library builds them on the device.
+template <class P, int TN>
+static std::vector<float4> thread_twiddles(const float2* roots) {
+    std::vector<float4> tab((size_t)P::TWU * P::kThreads);
+    for (int t = 0; t < P::kThreads; ++t) P::template fill_thread_twiddles<TN>(tab.data(), roots, t);
+    return tab;
+}
+template <int N>
+using RowPlanOf = zf::Stockham<N / 2, zf::fft_threads(N / 2), false, false>;
+template <int N>
+using ColPlanOf = zf::Stockham<N, zf::fft_threads(N), false, false>;
+template <int N>
+using RevPlanOf = zf::Stockham<N, zf::fft_threads(N), true, true>;
+
 template <int H, bool CONJ, int NZ>
 void run_col(float2* Q, const float2* R, int r_pitch, const float2* spec, const float2* tw, int h,
              int W2, int rows, int nt, long long qts, long long rts, int cap) {
     using C = zf::ColCfg<H, NZ>;
     int grid = (W2 + C::FPB) / C::FPB * nt;
     if (grid > cap) grid = cap;
+    const auto tt = thread_twiddles<ColPlanOf<H>, H>(tw);
+    const auto tr = thread_twiddles<RevPlanOf<H>, H>(tw);
     emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_col_fused<H, CONJ, NZ>, Q, R,
-               r_pitch, spec, tw, h, W2, rows, R != Q ? 1 : 0, nt, qts, rts, &g_status);
+               r_pitch, spec, tt.data(), tr.data(), h, W2, rows, R != Q ? 1 : 0, nt, qts, rts,
+               &g_status);
 }
 template <int W2, int NZ>
 void run_r2c(const float* tm, float2* R, const float2* tw, int h, int w, int r_pitch,
@@ -356,16 +470,18 @@ void run_r2c(const float* tm, float2* R, const float2* tw, int h, int w, int r_p
     using C = zf::R2cCfg<W2>;
     int units = ((h + 1) / 2 * 2 + C::RPB - 1) / C::RPB * nt;
     int grid = units < cap ? units : cap;
-    emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_row_r2c<W2, NZ>, tm, R, tw, h,
-               w, r_pitch, r_tstride, nt, sc);
+    const auto tt = thread_twiddles<RowPlanOf<2 * W2>, 2 * W2>(tw);
+    emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_row_r2c<W2, NZ>, tm, R, tw,
+               tt.data(), h, w, r_pitch, r_tstride, nt, sc);
 }
 template <int H>
 void run_col_fwd(float2* spec, const float2* tw, int W2, int cap) {
     using C = zf::ColFwdCfg<H>;
     int grid = (W2 + C::FPB - 1) / C::FPB;
     if (grid > cap) grid = cap;
-    emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_col_fwd<H>, spec, tw, W2,
-               &g_status);
+    const auto tt = thread_twiddles<ColPlanOf<H>, H>(tw);
+    emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_col_fwd<H>, spec, tt.data(),
+               W2, &g_status);
 }
 template <int W2>
 void run_c2r(const float2* Q, int H, float* out, int* arg, float* sum, float* sumsq,
@@ -375,34 +491,36 @@ void run_c2r(const float2* Q, int H, float* out, int* arg, float* sum, float* su
     zf::CUtensorMap map{reinterpret_cast<const unsigned char*>(Q), H, W2 * nt, (long long)H * 8,
                         C::RPB, C::BOXK, 8};
     int groups = (orows + C::RPB - 1) / C::RPB * nt;
+    const auto ttr = thread_twiddles<RowPlanOf<2 * W2>, 2 * W2>(tw);
+    const auto ttc = thread_twiddles<ColPlanOf<2 * W2>, 2 * W2>(tw);
     int grid = groups < cap ? groups : cap;
     float* nf = nullptr;
     unsigned* np = nullptr;
     if (arg && sum)
         emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM,
-                   zf::k_row_c2r<W2, zf::kRunningStats>, map, out, arg, sum, sumsq, np, tw, orows,
+                   zf::k_row_c2r<W2, zf::kRunningStats>, map, out, arg, sum, sumsq, np, tw, ttr.data(), orows,
                    ocols, ocols, tindex, reset, nt, ots, &g_status);
     else if (arg)
         emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_row_c2r<W2, zf::kRunningMax>,
-                   map, out, arg, nf, nf, np, tw, orows, ocols, ocols, tindex, reset, nt, ots,
+                   map, out, arg, nf, nf, np, tw, ttr.data(), orows, ocols, ocols, tindex, reset, nt, ots,
                    &g_status);
     else if (ocols == 2 * W2 && reinterpret_cast<uintptr_t>(out) % 8 == 0 && ots % 2 == 0) {
         // full aligned maps: the W/2-point form, as the library launches it
         if (peak)
             emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM,
-                       zf::k_row_c2r<W2, zf::kStorePeak>, map, out, (int*)nullptr, nf, nf, peak, tw,
+                       zf::k_row_c2r<W2, zf::kStorePeak>, map, out, (int*)nullptr, nf, nf, peak, tw, ttr.data(),
                        orows, ocols, ocols, 0, 0, nt, ots, &g_status);
         else
             emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM,
-                       zf::k_row_c2r<W2, zf::kStoreMap>, map, out, (int*)nullptr, nf, nf, np, tw,
+                       zf::k_row_c2r<W2, zf::kStoreMap>, map, out, (int*)nullptr, nf, nf, np, tw, ttr.data(),
                        orows, ocols, ocols, 0, 0, nt, ots, &g_status);
     } else if (peak)  // cropped maps: the row-pair form
         emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, zf::C2rPairCfg<W2>::SMEM,
-                   zf::k_row_c2r_pair<W2, zf::kStorePeak>, map, out, peak, tw, orows, ocols, ocols,
+                   zf::k_row_c2r_pair<W2, zf::kStorePeak>, map, out, peak, ttc.data(), orows, ocols, ocols,
                    nt, ots, &g_status);
     else
         emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, zf::C2rPairCfg<W2>::SMEM,
-                   zf::k_row_c2r_pair<W2, zf::kStoreMap>, map, out, np, tw, orows, ocols, ocols, nt,
+                   zf::k_row_c2r_pair<W2, zf::kStoreMap>, map, out, np, ttc.data(), orows, ocols, ocols, nt,
                    ots, &g_status);
 }
 

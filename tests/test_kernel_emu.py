@@ -29,9 +29,13 @@ def emu():
         pytest.skip("g++ not available")
     if not os.path.exists(EXE) or os.path.getmtime(EXE) < _deps():
         os.makedirs(os.path.dirname(EXE), exist_ok=True)
+        # Build under a private name and rename: parallel test workers may
+        # build at the same time, and none may run a half-written binary.
+        tmp = f"{EXE}.{os.getpid()}.tmp"
         subprocess.check_call(["g++", "-std=c++20", "-O1", "-g", "-fsanitize=address,alignment",
                                "-fno-sanitize-recover=alignment", "-fno-omit-frame-pointer",
-                               "-pthread", SRC, "-o", EXE])
+                               "-pthread", SRC, "-o", tmp])
+        os.replace(tmp, EXE)
     return EXE
 
 

@@ -77,6 +77,28 @@ def test_2dtm_sizes_sampled_templates(H, h, B, check):
         assert_parity(ref, out[b], what=f"{H}^2 / {h}^2 template {b}")
 
 
+@pytest.mark.parametrize("which", ["soft_mask_256", "gaussian_blob_512"])
+def test_baseline_template_content(which):
+    """The measured workloads' own template content, not plain N(0,1): 256^2
+    templates times the soft circular mask (radius 112 px + 8 px raised
+    cosine), and 512^2 Gaussian blobs (sigma 20 px) plus N(0, 0.1) noise,
+    each zero-mean unit-variance, in a 4096^2 image; sampled templates
+    against the oracle."""
+    from bench import gaussian_blob_templates, make_templates
+
+    H = 4096
+    if which == "soft_mask_256":
+        tm, check = make_templates(8, 1), (0, 5, 7)
+    else:
+        tm, check = gaussian_blob_templates(4, 512, 20.0, 0.1, 1), (0, 3)
+    g = torch.Generator().manual_seed(0)
+    spec = torch.from_numpy(O.image_spectrum_T(torch.randn((H, H), generator=g).numpy()))
+    out = capi_corr(tm, spec, H, H, True)
+    for b in check:
+        ref = O.padded_corr2d_f64(tm[b].numpy(), spec.numpy(), H, H, True, True)
+        assert_parity(ref, out[b], what=f"{which} template {b}")
+
+
 def test_linearity_full_size():
     """corr(a T1 + b T2) = a corr(T1) + b corr(T2) at 4096^2 / 256^2."""
     H = 4096
@@ -229,6 +251,26 @@ def test_corr_peaks_equal_map_maxima(B, sy, sx, H, W, full):
         zipfft.padded_rconv2d.corr(tm_d[0], ws[0], sp_d, out[0], H, W, peaks=p1)
         torch.cuda.synchronize()
         assert torch.equal(p1, peaks)
+
+
+def test_corr_peaks_propagate_nan_like_amax():
+    """A template holding a NaN makes its whole map NaN (every output mixes
+    every input); its peak is NaN, as torch.amax of that map is, and the
+    other templates' peaks are unaffected."""
+    import zipfft
+
+    B, sy, sx, H, W = 3, 16, 16, 256, 256
+    _, tm, spec = make_inputs(B, sy, sx, H, W, seed=21)
+    tm[1, 3, 5] = float("nan")
+    dev = torch.device("cuda", 0)
+    ws = torch.empty((B, H, W // 2 + 1), dtype=torch.complex64, device=dev)
+    out = torch.empty((B, H, W), device=dev)
+    peaks = torch.zeros((B,), device=dev)
+    zipfft.padded_rconv2d.corr(tm.to(dev), ws, spec.to(dev), out, H, W, peaks=peaks)
+    torch.cuda.synchronize()
+    amax = out.reshape(B, -1).amax(dim=1)
+    assert torch.isnan(out[1]).all() and torch.isnan(amax[1]) and torch.isnan(peaks[1])
+    assert torch.equal(peaks[[0, 2]], amax[[0, 2]])
 
 
 def test_corr_peaks_argument_errors():

@@ -92,3 +92,54 @@ def test_validation_order_and_messages(monkeypatch):
         v(bi, bws[:2], bcd, bout)
     with pytest.raises(RuntimeError, match="must be contiguous"):
         v(bi.transpose(1, 2), bws, bcd, bout)
+
+
+def test_expanded_output_rejected_before_launch(monkeypatch):
+    """An output expanded over the batch (stride 0) would make the kernels
+    write B maps into one map's storage: corr and conv reject it with the
+    contiguity error before anything is launched; only corr_max's internal
+    shape stand-in skips that check."""
+    from zipfft_b200 import _lib
+    from zipfft_b200 import padded_rconv2d as P
+
+    class FakeDev:
+        type = "cuda"
+        index = 0
+
+        def __eq__(self, other):
+            return True
+
+    class Wrap:
+        def __init__(self, t):
+            self.t = t
+            self.device = FakeDev()
+
+        def __getattr__(self, k):
+            return getattr(self.t, k)
+
+    real_validate = P._validate
+
+    def validate_wrapped(*a, **k):
+        return real_validate(*(Wrap(x) if isinstance(x, torch.Tensor) else x for x in a), **k)
+
+    def no_launch():
+        raise AssertionError("the library was reached with an invalid output")
+
+    monkeypatch.setattr(P, "_validate", validate_wrapped)
+    monkeypatch.setattr(_lib, "load", no_launch)
+    bi, bws, bcd, _ = tensors(B=3)
+    expanded = torch.zeros(64, 64).expand(3, 64, 64)
+    assert expanded.stride(0) == 0
+    for fn in (P.corr, P.conv):
+        with pytest.raises(RuntimeError, match="Output tensor must be contiguous"):
+            fn(bi, bws, bcd, expanded, 64, 64)
+    with pytest.raises(RuntimeError, match="Output tensor must be contiguous"):
+        P.corr(bi, bws, bcd, expanded, 64, 64, peaks=torch.zeros(3))
+    # an overlapping (non-expanded but strided) output is rejected the same way
+    base = torch.zeros(3 * 64 + 64, 64)
+    overlap = base.as_strided((3, 64, 64), (64, 64, 1))
+    with pytest.raises(RuntimeError, match="Output tensor must be contiguous"):
+        P.corr(bi, bws, bcd, overlap, 64, 64)
+    # corr_max's stand-in (not an output the kernels write) passes the checks
+    assert real_validate(Wrap(bi), Wrap(bws), Wrap(bcd), Wrap(expanded), 64, 64,
+                         output_is_shape_stand_in=True)[0] == 3

@@ -38,15 +38,33 @@ def noalloc_corr(tm, spec, H, W, full):
     return out.cpu().numpy()
 
 
+# (B, h, w, H, W, full, seed).  The fixed 16 MiB array is laid out by the
+# same rules as a caller's workspace of that size, so the cases cover each
+# layout it can take: the intermediate alone (2048^2), the row spectra of a
+# chunk of templates after it (1920 x 2048: one 15 MiB slice plus 1 MiB), and
+# batched groups of several slices (1024 x 2048, 512^2).  The workspace entry
+# point is given exactly one slice, so it always runs templates one by one.
+NOALLOC_CASES = [
+    (3, 100, 80, 2048, 2048, True, 1),
+    (2, 37, 53, 1024, 2048, False, 2),
+    (4, 37, 29, 1920, 2048, True, 4),
+    (8, 48, 48, 512, 512, True, 5),
+]
+
+
 def test_noalloc_matches_workspace_entry_point_on_two_calls():
-    # Two calls in a row with different shapes and inputs: the second runs on
-    # the scratch array as the first left it.
-    for (B, h, w, H, W, full, seed) in [(3, 100, 80, 2048, 2048, True, 1),
-                                        (2, 37, 53, 1024, 2048, False, 2)]:
+    # Calls in a row with different shapes and inputs: each runs on the
+    # scratch array as the previous call left it.  Results do not depend on
+    # the workspace layout, so they equal the workspace entry point's bit for
+    # bit; the oracle pins both.
+    for (B, h, w, H, W, full, seed) in NOALLOC_CASES:
         _, tm, spec = make_inputs(B, h, w, H, W, seed=seed)
         got = noalloc_corr(tm, spec, H, W, full)
         want = capi_corr(tm, spec, H, W, full, True)
-        assert_parity(want, got, what=f"no-alloc vs workspace entry point {(B, h, w, H, W)}")
+        what = f"no-alloc entry point {(B, h, w, H, W)}"
+        assert np.array_equal(want, got), f"{what}: differs from the workspace entry point"
+        assert_parity(O.padded_corr2d_f64(tm.numpy(), spec.numpy(), H, W, True, full), got,
+                      what=what)
     assert _lib.check_device_status(0) == 0
 
 

@@ -141,6 +141,16 @@ int ensure_device(int device) {
     e = cudaGetSymbolAddress(&p, g_status);
     if (e != cudaSuccess) return cuda_fail(e, "resolving device status address");
     g_dev_status[device] = static_cast<int*>(p);
+    // Per-thread twiddle tables of every size's kernels, built on the device
+    // from the root tables (once; this first call synchronizes the device).
+#define ZF_X(N)                                                                   \
+    if ((e = zf::init_thread_twiddles_##N(g_dev_pool[device] + tw_offset(N), device)) != \
+        cudaSuccess)                                                              \
+        return cuda_fail(e, "building the per-thread twiddle tables");
+    ZF_FOR_EACH_FFT_SIZE(ZF_X)
+#undef ZF_X
+    if ((e = cudaDeviceSynchronize()) != cudaSuccess)
+        return cuda_fail(e, "building the per-thread twiddle tables");
     g_dev_ready[device] = true;
     return ZFFT_SUCCESS;
 }

@@ -88,6 +88,16 @@ constexpr double cx_sin2pi(long m, long n) {
 
 // ---------------------------------------------------------------------------
 // Complex helpers (float2 = {re, im})
+//
+// Sums, differences and products by constants run as packed f32x2
+// instructions on the device (FADD2 / FMUL2 / FFMA2: one instruction for both
+// lanes; an operand may broadcast or swap the halves of its register pair and
+// be negated at no cost, measured with ncu on sm_100a).  The packed forms give
+// the FP32 pipe the same work (it retires 128 lanes per clock per SM either
+// way) in half the issue slots.  A product of two variable complex values
+// needs a different sign in each lane, which no operand modifier provides, so
+// c_mul and friends stay scalar (two FMUL + two FFMA).  Host compilation (the
+// CPU test harness) computes the same lanes with scalar IEEE operations.
 // ---------------------------------------------------------------------------
 ZF_HD float2 c_make(float re, float im) {
     float2 r;
@@ -95,11 +105,24 @@ ZF_HD float2 c_make(float re, float im) {
     r.y = im;
     return r;
 }
-ZF_HD float2 c_add(float2 a, float2 b) { return c_make(a.x + b.x, a.y + b.y); }
-ZF_HD float2 c_sub(float2 a, float2 b) { return c_make(a.x - b.x, a.y - b.y); }
+#if defined(__CUDA_ARCH__)
+// lane-wise a + b, a * b, a * b + c (round to nearest)
+ZF_DEV float2 px_add(float2 a, float2 b) { return __fadd2_rn(a, b); }
+ZF_DEV float2 px_mul(float2 a, float2 b) { return __fmul2_rn(a, b); }
+ZF_DEV float2 px_fma(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+#else
+ZF_HD float2 px_add(float2 a, float2 b) { return c_make(a.x + b.x, a.y + b.y); }
+ZF_HD float2 px_mul(float2 a, float2 b) { return c_make(a.x * b.x, a.y * b.y); }
+ZF_HD float2 px_fma(float2 a, float2 b, float2 c) {
+    return c_make(fmaf(a.x, b.x, c.x), fmaf(a.y, b.y, c.y));
+}
+#endif
+ZF_HD float2 c_swap(float2 a) { return c_make(a.y, a.x); }
+ZF_HD float2 c_add(float2 a, float2 b) { return px_add(a, b); }
+ZF_HD float2 c_sub(float2 a, float2 b) { return px_add(a, c_make(-b.x, -b.y)); }
 ZF_HD float2 c_neg(float2 a) { return c_make(-a.x, -a.y); }
 ZF_HD float2 c_conj(float2 a) { return c_make(a.x, -a.y); }
-ZF_HD float2 c_scale(float2 a, float s) { return c_make(a.x * s, a.y * s); }
+ZF_HD float2 c_scale(float2 a, float s) { return px_mul(a, c_make(s, s)); }
 // a * b, each component with one fused multiply-add.
 ZF_HD float2 c_mul(float2 a, float2 b) {
     return c_make(fmaf(a.x, b.x, -a.y * b.y), fmaf(a.x, b.y, a.y * b.x));
@@ -119,9 +142,30 @@ ZF_HD float2 c_rot(float2 a) {
 }
 // a * i
 ZF_HD float2 c_mul_i(float2 a) { return c_make(-a.y, a.x); }
+// t + rot<INV>(d) and t - rot<INV>(d): one packed FMA of the swapped d.
+template <bool INV>
+ZF_HD float2 c_add_rot(float2 t, float2 d) {
+    return px_fma(c_swap(d), INV ? c_make(-1.f, 1.f) : c_make(1.f, -1.f), t);
+}
+template <bool INV>
+ZF_HD float2 c_sub_rot(float2 t, float2 d) {
+    return px_fma(c_swap(d), INV ? c_make(1.f, -1.f) : c_make(-1.f, 1.f), t);
+}
+// t + s * rot<INV>(d) for a real constant s.
+template <bool INV>
+ZF_HD float2 c_add_rot_scaled(float2 t, float2 d, float s) {
+    return px_fma(c_swap(d), INV ? c_make(-s, s) : c_make(s, -s), t);
+}
+// a * (wr + i wi) for constants: two packed instructions (the broadcast
+// halves of a against (wr, wi) and (-wi, wr)).
+ZF_HD float2 c_mul_const(float2 a, float wr, float wi) {
+    return px_fma(c_make(a.x, a.x), c_make(wr, wi), px_mul(c_make(a.y, a.y), c_make(-wi, wr)));
+}
 
 // Multiply by the compile-time root of unity exp(-+2 pi i M / N) (forward sign
-// "-", inverse sign "+").  Exact special cases avoid multiplications.
+// "-", inverse sign "+").  Exact special cases avoid multiplications.  A
+// quarter turn (+-i) costs an instruction of its own here; the butterflies
+// below fold those into the following sum instead (c_add_rot / c_sub_rot).
 template <int M, int N, bool INV>
 ZF_HD float2 c_mul_w(float2 a) {
     constexpr int m0 = ((M % N) + N) % N;
@@ -134,23 +178,25 @@ ZF_HD float2 c_mul_w(float2 a) {
         return c_make(a.y, -a.x);  // * (-i)
     } else if constexpr (4 * m == 3 * N) {
         return c_make(-a.y, a.x);  // * (+i)
-    } else if constexpr (8 * m == N) {
-        constexpr float c = 0.70710678118654752440f;  // (1 - i)/sqrt2
-        return c_make(c * (a.x + a.y), c * (a.y - a.x));
-    } else if constexpr (8 * m == 3 * N) {
-        constexpr float c = 0.70710678118654752440f;  // (-1 - i)/sqrt2
-        return c_make(c * (a.y - a.x), -c * (a.x + a.y));
-    } else if constexpr (8 * m == 5 * N) {
-        constexpr float c = 0.70710678118654752440f;  // (-1 + i)/sqrt2
-        return c_make(-c * (a.x + a.y), c * (a.x - a.y));
-    } else if constexpr (8 * m == 7 * N) {
-        constexpr float c = 0.70710678118654752440f;  // (1 + i)/sqrt2
-        return c_make(c * (a.x - a.y), c * (a.x + a.y));
     } else {
         constexpr float wr = float(cx_cos2pi(m, N));
         constexpr float wi = float(-cx_sin2pi(m, N));
-        return c_mul(a, c_make(wr, wi));
+        return c_mul_const(a, wr, wi);
     }
+}
+// True when c_mul_w<M, N, INV> is a quarter turn (then equal to c_rot<Q>
+// with Q = quarter_turn_inv<M, N, INV>()).
+template <int M, int N, bool INV>
+constexpr bool is_quarter_turn() {
+    constexpr int m0 = ((M % N) + N) % N;
+    constexpr int m = INV ? (N - m0) % N : m0;
+    return 4 * m == N || 4 * m == 3 * N;
+}
+template <int M, int N, bool INV>
+constexpr bool quarter_turn_inv() {  // +i (true) or -i (false)
+    constexpr int m0 = ((M % N) + N) % N;
+    constexpr int m = INV ? (N - m0) % N : m0;
+    return 4 * m == 3 * N;
 }
 
 // Calls f(std::integral_constant<int, I>) for I = 0 .. N-1 (compile-time index).
@@ -174,16 +220,24 @@ ZF_HD void dft2(float2& a, float2& b) {
     b = c_sub(t, b);
 }
 
-template <bool INV>
+// 4-point DFT; with ROT2 the input a2 arrives unrotated and is multiplied by
+// rot<INV> (a quarter turn) inside, folded into the first sums.
+template <bool INV, bool ROT2 = false>
 ZF_HD void dft4(float2& a0, float2& a1, float2& a2, float2& a3) {
-    float2 t0 = c_add(a0, a2);
-    float2 t1 = c_sub(a0, a2);
-    float2 t2 = c_add(a1, a3);
-    float2 t3 = c_rot<INV>(c_sub(a1, a3));
+    float2 t0, t1;
+    if constexpr (ROT2) {
+        t0 = c_add_rot<INV>(a0, a2);
+        t1 = c_sub_rot<INV>(a0, a2);
+    } else {
+        t0 = c_add(a0, a2);
+        t1 = c_sub(a0, a2);
+    }
+    const float2 t2 = c_add(a1, a3);
+    const float2 t3 = c_sub(a1, a3);
     a0 = c_add(t0, t2);
     a2 = c_sub(t0, t2);
-    a1 = c_add(t1, t3);
-    a3 = c_sub(t1, t3);
+    a1 = c_add_rot<INV>(t1, t3);
+    a3 = c_sub_rot<INV>(t1, t3);
 }
 
 // 8 = 4 x 2 Cooley-Tukey: DFT4 on even/odd halves, twiddle, DFT2.
@@ -192,17 +246,16 @@ ZF_HD void dft8(float2* v) {
     dft4<INV>(v[0], v[2], v[4], v[6]);  // E[k1] at v[0],v[2],v[4],v[6]
     dft4<INV>(v[1], v[3], v[5], v[7]);  // O[k1] at v[1],v[3],v[5],v[7]
     v[3] = c_mul_w<1, 8, INV>(v[3]);
-    v[5] = c_mul_w<2, 8, INV>(v[5]);
     v[7] = c_mul_w<3, 8, INV>(v[7]);
-    // X[k1] = E + w O, X[k1+4] = E - w O
+    // X[k1] = E + w O, X[k1+4] = E - w O (w_8^2 = rot<INV>, folded)
     float2 e0 = v[0], e1 = v[2], e2 = v[4], e3 = v[6];
     float2 o0 = v[1], o1 = v[3], o2 = v[5], o3 = v[7];
     v[0] = c_add(e0, o0);
     v[4] = c_sub(e0, o0);
     v[1] = c_add(e1, o1);
     v[5] = c_sub(e1, o1);
-    v[2] = c_add(e2, o2);
-    v[6] = c_sub(e2, o2);
+    v[2] = c_add_rot<INV>(e2, o2);
+    v[6] = c_sub_rot<INV>(e2, o2);
     v[3] = c_add(e3, o3);
     v[7] = c_sub(e3, o3);
 }
@@ -215,12 +268,12 @@ ZF_HD void dft16(float2* v) {
     dft4<INV>(v[1], v[5], v[9], v[13]);
     dft4<INV>(v[2], v[6], v[10], v[14]);
     dft4<INV>(v[3], v[7], v[11], v[15]);
-    // Step 2: twiddle slot (4 k1 + n2) by w16^(n2 k1).
+    // Step 2: twiddle slot (4 k1 + n2) by w16^(n2 k1) (w16^4 = rot<INV> is
+    // folded into step 3).
     v[5] = c_mul_w<1, 16, INV>(v[5]);
     v[9] = c_mul_w<2, 16, INV>(v[9]);
     v[13] = c_mul_w<3, 16, INV>(v[13]);
     v[6] = c_mul_w<2, 16, INV>(v[6]);
-    v[10] = c_mul_w<4, 16, INV>(v[10]);
     v[14] = c_mul_w<6, 16, INV>(v[14]);
     v[7] = c_mul_w<3, 16, INV>(v[7]);
     v[11] = c_mul_w<6, 16, INV>(v[11]);
@@ -229,7 +282,7 @@ ZF_HD void dft16(float2* v) {
     // X[k1 + 4 k2].
     dft4<INV>(v[0], v[1], v[2], v[3]);
     dft4<INV>(v[4], v[5], v[6], v[7]);
-    dft4<INV>(v[8], v[9], v[10], v[11]);
+    dft4<INV, true>(v[8], v[9], v[10], v[11]);
     dft4<INV>(v[12], v[13], v[14], v[15]);
     // Slot 4 k1 + k2 now holds X[k1 + 4 k2]: transpose the 4 x 4 index grid.
     float2 t;
@@ -244,14 +297,13 @@ ZF_HD void dft16(float2* v) {
 template <bool INV>
 ZF_HD void dft3(float2* v) {
     constexpr float s3 = 0.86602540378443864676f;  // sin(2 pi / 3)
-    float2 t1 = c_add(v[1], v[2]);
-    float2 t2 = c_make(fmaf(-0.5f, t1.x, v[0].x), fmaf(-0.5f, t1.y, v[0].y));
-    float2 d = c_sub(v[1], v[2]);
-    // forward: t3 = -i s3 d ; inverse: +i s3 d
-    float2 t3 = c_rot<INV>(c_scale(d, s3));
+    const float2 t1 = c_add(v[1], v[2]);
+    const float2 t2 = px_fma(t1, c_make(-0.5f, -0.5f), v[0]);
+    const float2 d = c_sub(v[1], v[2]);
+    // forward: X1 = t2 - i s3 d, X2 = t2 + i s3 d (inverse: signs swapped)
     v[0] = c_add(v[0], t1);
-    v[1] = c_add(t2, t3);
-    v[2] = c_sub(t2, t3);
+    v[1] = c_add_rot_scaled<INV>(t2, d, s3);
+    v[2] = c_add_rot_scaled<INV>(t2, d, -s3);
 }
 
 template <bool INV>
@@ -260,23 +312,21 @@ ZF_HD void dft5(float2* v) {
     constexpr float c2 = float(cx_cos2pi(2, 5));
     constexpr float s1 = float(cx_sin2pi(1, 5));
     constexpr float s2 = float(cx_sin2pi(2, 5));
-    float2 a0 = v[0];
-    float2 t1 = c_add(v[1], v[4]);
-    float2 t2 = c_add(v[2], v[3]);
-    float2 t3 = c_sub(v[1], v[4]);
-    float2 t4 = c_sub(v[2], v[3]);
-    float2 m1 = c_make(fmaf(c1, t1.x, fmaf(c2, t2.x, a0.x)), fmaf(c1, t1.y, fmaf(c2, t2.y, a0.y)));
-    float2 m2 = c_make(fmaf(c2, t1.x, fmaf(c1, t2.x, a0.x)), fmaf(c2, t1.y, fmaf(c1, t2.y, a0.y)));
-    float2 n1 = c_make(fmaf(s1, t3.x, s2 * t4.x), fmaf(s1, t3.y, s2 * t4.y));
-    float2 n2 = c_make(fmaf(s2, t3.x, -s1 * t4.x), fmaf(s2, t3.y, -s1 * t4.y));
+    const float2 a0 = v[0];
+    const float2 t1 = c_add(v[1], v[4]);
+    const float2 t2 = c_add(v[2], v[3]);
+    const float2 t3 = c_sub(v[1], v[4]);
+    const float2 t4 = c_sub(v[2], v[3]);
+    const float2 m1 = px_fma(t1, c_make(c1, c1), px_fma(t2, c_make(c2, c2), a0));
+    const float2 m2 = px_fma(t1, c_make(c2, c2), px_fma(t2, c_make(c1, c1), a0));
+    const float2 n1 = px_fma(t3, c_make(s1, s1), px_mul(t4, c_make(s2, s2)));
+    const float2 n2 = px_fma(t3, c_make(s2, s2), px_mul(t4, c_make(-s1, -s1)));
     // forward: X1 = m1 - i n1, X4 = m1 + i n1, X2 = m2 - i n2, X3 = m2 + i n2
-    float2 r1 = c_rot<INV>(n1);
-    float2 r2 = c_rot<INV>(n2);
     v[0] = c_add(a0, c_add(t1, t2));
-    v[1] = c_add(m1, r1);
-    v[4] = c_sub(m1, r1);
-    v[2] = c_add(m2, r2);
-    v[3] = c_sub(m2, r2);
+    v[1] = c_add_rot<INV>(m1, n1);
+    v[4] = c_sub_rot<INV>(m1, n1);
+    v[2] = c_add_rot<INV>(m2, n2);
+    v[3] = c_sub_rot<INV>(m2, n2);
 }
 
 // 15-point DFT by the prime-factor (Good-Thomas) algorithm, 15 = 3 x 5 with
@@ -330,7 +380,8 @@ ZF_HD void dft(float2* v) {
 
 // ---------------------------------------------------------------------------
 // Stockham plan: N = product of radices, largest first (16s, then the left-over
-// power of two, then 15s, 5s and 3s; 16 x 16 x 15 is ordered 16, 15, 16).
+// power of two, then 15s, 5s and 3s), except that a three-stage plan
+// 16 x 16 x r is ordered 16, r, 16.
 // ---------------------------------------------------------------------------
 struct PlanInfo {
     int S;
@@ -369,10 +420,11 @@ constexpr PlanInfo make_plan(int n) {
         p.R[p.S++] = 3;
         n /= 3;
     }
-    // 16, 16, 15 -> 16, 15, 16: a palindromic plan, whose reversed inverse
-    // shares the forward transform's twiddles.
-    if (p.S == 3 && p.R[0] == 16 && p.R[1] == 16 && p.R[2] == 15) {
-        p.R[1] = 15;
+    // 16, 16, r -> 16, r, 16 (r = 2, 4, 8 or 15): a palindromic plan, whose
+    // reversed inverse shares the forward transform's twiddles (the column
+    // pass then holds one twiddle set instead of two).
+    if (p.S == 3 && p.R[0] == 16 && p.R[1] == 16) {
+        p.R[1] = p.R[2];
         p.R[2] = 16;
     }
     return p;
@@ -395,6 +447,7 @@ template <int N, int T, bool INV, bool REV>
 struct Stockham {
     static constexpr PlanInfo P = make_plan(N);
     static constexpr int S = P.S;
+    static constexpr int kThreads = T;
     static_assert(fft_size_factorable(N), "FFT size must be 2^a 3^b 5^c >= 16");
 
     static constexpr int radix(int s) { return REV ? P.R[S - 1 - s] : P.R[s]; }
@@ -462,6 +515,48 @@ struct Stockham {
                 }
             }
             load_twiddles_stage<s + 1, TN>(tw, table, t);
+        }
+    }
+
+    // ---- per-thread twiddle tables --------------------------------------
+    // A thread's NTW twiddles followed by its NR0 pruned-start roots, in
+    // pairs: unit j (float4) of thread t at tab[j * T + t], so that a warp's
+    // load of unit j is one contiguous 512-byte request (loading from the
+    // shared root table touches up to 32 sectors per request, at every
+    // launch).  fill_thread_twiddles builds a thread's units with
+    // load_twiddles itself, so the values are the same.
+    static constexpr int NR0 = bpt(S > 1 ? 1 : 0);
+    static constexpr int TWU = (NTW + NR0 + 1) / 2;
+    ZF_HD static float2 tw_get(const Twiddles& tw, int k) {
+        return k < NTW ? tw.w[k] : tw.r0[k - NTW];
+    }
+    ZF_HD static void tw_set(Twiddles& tw, int k, float2 v) {
+        if (k < NTW)
+            tw.w[k] = v;
+        else
+            tw.r0[k - NTW] = v;
+    }
+    template <int TN>
+    ZF_DEV static void fill_thread_twiddles(float4* tab, const float2* __restrict__ table, int t) {
+        Twiddles tw;
+        load_twiddles<TN>(tw, table, t);
+        for (int j = 0; j < TWU; ++j) {
+            const float2 a = tw_get(tw, 2 * j);
+            const float2 b = 2 * j + 1 < NTW + NR0 ? tw_get(tw, 2 * j + 1) : c_make(0.f, 0.f);
+            float4 u;
+            u.x = a.x;
+            u.y = a.y;
+            u.z = b.x;
+            u.w = b.y;
+            tab[j * T + t] = u;
+        }
+    }
+    ZF_DEV static void load_thread_twiddles(Twiddles& tw, const float4* __restrict__ tab, int t) {
+#pragma unroll
+        for (int j = 0; j < TWU; ++j) {
+            const float4 u = __ldg(tab + j * T + t);
+            tw_set(tw, 2 * j, c_make(u.x, u.y));
+            if (2 * j + 1 < NTW + NR0) tw_set(tw, 2 * j + 1, c_make(u.z, u.w));
         }
     }
 
@@ -567,18 +662,23 @@ struct Stockham {
         run_from<1>(v, buf, tw, t);
     }
 
-    // Full forward transform of a zero-padded input given by a loader
-    // ld(i) -> x[i] (the loader returns zero past the signal end).  NZ is the
-    // number of possibly non-zero inputs per stage-0 butterfly (0 = unknown):
-    // for NZ in {1, 2} stage 0 is folded into the reads of stage 1, so the
-    // padded region is neither read nor transformed.
-    // The twiddle set TWS is this transform's Twiddles, or that of a transform
-    // with the same radix sequence (a palindromic plan run in reverse).
+    // Stage at which a transform of a zero-padded input starts computing: 1
+    // when stage 0 folds into the reads of stage 1 (NZ in {1, 2}), else 0.
+    template <int NZ>
+    static constexpr int first_stage() {
+        return ((NZ == 1 || NZ == 2) && S >= 2) ? 1 : 0;
+    }
+
+    // Inputs of stage first_stage<NZ>() of a forward transform of a
+    // zero-padded input given by a loader ld(i) -> x[i] (the loader returns
+    // zero past the signal end).  NZ is the number of possibly non-zero
+    // inputs per stage-0 butterfly (0 = unknown): for NZ in {1, 2} stage 0 is
+    // folded into the reads of stage 1, so the padded region is neither read
+    // nor transformed.
     template <int NZ, class LD, class TWS>
-    ZF_DEV static void run_loader(float2 (&v)[MAXE], const LD& ld, float2* buf, const TWS& tw,
-                                  int t) {
+    ZF_DEV static void load_input(float2 (&v)[MAXE], const LD& ld, const TWS& tw, int t) {
         constexpr int R0 = radix(0), NB0 = nbf(0);
-        if constexpr ((NZ == 1 || NZ == 2) && S >= 2) {
+        if constexpr (first_stage<NZ>() == 1) {
             // Stage-1 input i equals stage-0 output (butterfly m = i / R0,
             // element k = i % R0) = sum_{j < NZ} x[m + j NB0] w_R0^{j k}.
             // Since R0 divides N/R1, k = b mod R0 for every element of
@@ -599,8 +699,6 @@ struct Stockham {
                     }
                 }
             }
-            compute<1>(v, tw);
-            run_from<2>(v, buf, tw, t);
         } else {
 #pragma unroll
             for (int q = 0; q < bpt(0); ++q) {
@@ -610,7 +708,22 @@ struct Stockham {
                     for (int r = 0; r < R0; ++r) v[q * R0 + r] = ld(b + r * NB0);
                 }
             }
-            run_regs(v, buf, tw, t);
+        }
+    }
+
+    // Full forward transform of a zero-padded input given by a loader (see
+    // load_input).  The twiddle set TWS is this transform's Twiddles, or that
+    // of a transform with the same radix sequence (a palindromic plan run in
+    // reverse).  TAIL as in run_from.
+    template <int NZ, bool TAIL = true, class LD, class TWS>
+    ZF_DEV static void run_loader(float2 (&v)[MAXE], const LD& ld, float2* buf, const TWS& tw,
+                                  int t) {
+        load_input<NZ>(v, ld, tw, t);
+        if constexpr (first_stage<NZ>() == 1) {
+            compute<1>(v, tw);
+            run_from<2, TAIL>(v, buf, tw, t);
+        } else {
+            run_regs<TAIL>(v, buf, tw, t);
         }
     }
 };

@@ -50,6 +50,36 @@ cudaError_t configure(Kern kernel, KernelState& st, int smem, int threads, int d
 
 inline int min_int(int a, int b) { return a < b ? a : b; }
 
+// Per-thread twiddle tables of this size's kernels (Stockham::fill_thread_twiddles),
+// filled once per device by init_thread_twiddles_<n> from the size's root table:
+//   row: the W/2-point plan of the row kernels (k_row_r2c, k_row_c2r);
+//   col: the n-point plan (k_col_fused's forward transform, k_col_fwd, k_row_c2r_pair);
+//   rev: the n-point plan reversed (k_col_fused's inverse when the plan is not a palindrome).
+using RowPlan = Stockham<ZF_SIZE / 2, fft_threads(ZF_SIZE / 2), false, false>;
+using ColPlan = Stockham<ZF_SIZE, fft_threads(ZF_SIZE), false, false>;
+using RevPlan = Stockham<ZF_SIZE, fft_threads(ZF_SIZE), true, true>;
+__device__ float4 g_tt_row[RowPlan::TWU * RowPlan::kThreads];
+__device__ float4 g_tt_col[ColPlan::TWU * ColPlan::kThreads];
+__device__ float4 g_tt_rev[RevPlan::TWU * RevPlan::kThreads];
+constexpr int kTtThreads = cmax(RowPlan::kThreads, ColPlan::kThreads);
+
+__global__ void k_fill_thread_twiddles(const float2* __restrict__ roots) {
+    const int t = threadIdx.x;
+    if (blockIdx.x == 0 && t < RowPlan::kThreads)
+        RowPlan::template fill_thread_twiddles<ZF_SIZE>(g_tt_row, roots, t);
+    if (blockIdx.x == 1 && t < ColPlan::kThreads)
+        ColPlan::template fill_thread_twiddles<ZF_SIZE>(g_tt_col, roots, t);
+    if (blockIdx.x == 2 && t < RevPlan::kThreads)
+        RevPlan::template fill_thread_twiddles<ZF_SIZE>(g_tt_rev, roots, t);
+}
+
+struct ThreadTwiddles {
+    const float4* row = nullptr;
+    const float4* col = nullptr;
+    const float4* rev = nullptr;
+};
+ThreadTwiddles g_tt[kMaxDevices];  // device addresses, set by init_thread_twiddles
+
 // Launch with programmatic stream serialization: the kernel may start while
 // the previous kernel of the stream finishes; it calls griddepcontrol.wait
 // before touching that kernel's data.
@@ -81,8 +111,8 @@ cudaError_t r2c_t(const float* tmpl, float2* R, const float2* tw, int h, int w, 
     // One wave of co-resident blocks over all (template, row group) pairs.
     const long long units = (long long)((h + 1) / 2 * 2 + C::RPB - 1) / C::RPB * ntemplates;
     const int grid = (int)(units < cap ? units : cap);
-    return launch_pdl(kernel, dim3(grid > 0 ? grid : 1), C::THREADS, C::SMEM, s, tmpl, R, tw, h, w,
-                      r_pitch, r_tstride, ntemplates, scale);
+    return launch_pdl(kernel, dim3(grid > 0 ? grid : 1), C::THREADS, C::SMEM, s, tmpl, R, tw,
+                      g_tt[device].row, h, w, r_pitch, r_tstride, ntemplates, scale);
 }
 
 template <int H, bool CONJ, int NZ>
@@ -98,8 +128,9 @@ cudaError_t col_t(float2* Q, const float2* R, int r_pitch, const float2* spec, c
     if (e != cudaSuccess) return e;
     const long long units = (long long)((W2 + C::FPB) / C::FPB) * ntemplates;
     const int grid = (int)(units < cap ? units : cap);
-    return launch_pdl(kernel, dim3(grid), C::THREADS, C::SMEM, s, Q, R, r_pitch, spec, tw, h, W2,
-                      store_rows, discard_r ? 1 : 0, ntemplates, q_tstride, r_tstride, status);
+    return launch_pdl(kernel, dim3(grid), C::THREADS, C::SMEM, s, Q, R, r_pitch, spec,
+                      g_tt[device].col, g_tt[device].rev, h, W2, store_rows, discard_r ? 1 : 0,
+                      ntemplates, q_tstride, r_tstride, status);
 }
 
 template <int H>
@@ -112,7 +143,8 @@ cudaError_t col_fwd_t(float2* spec, const float2* tw, int W2, int* status, int d
     cudaError_t e = configure(kernel, st, C::SMEM, C::THREADS, device, &cap);
     if (e != cudaSuccess) return e;
     const int grid = min_int((W2 + C::FPB - 1) / C::FPB, cap);
-    return launch_pdl(kernel, dim3(grid), C::THREADS, C::SMEM, s, spec, tw, W2, status);
+    return launch_pdl(kernel, dim3(grid), C::THREADS, C::SMEM, s, spec, g_tt[device].col, W2,
+                      status);
 }
 
 template <int W2, int MODE>
@@ -129,8 +161,8 @@ cudaError_t c2r_t(const CUtensorMap* qmap, float* out, int* arg, float* sum, flo
     const long long units = (long long)((out_rows + C::RPB - 1) / C::RPB) * ntemplates;
     const int grid = (int)(units < cap ? units : cap);
     return launch_pdl(kernel, dim3(grid), C::THREADS, C::SMEM, s, *qmap, out, arg, sum, sumsq, peak,
-                      tw, out_rows, out_cols, out_pitch, tindex, reset, ntemplates, out_tstride,
-                      status);
+                      tw, g_tt[device].row, out_rows, out_cols, out_pitch, tindex, reset,
+                      ntemplates, out_tstride, status);
 }
 
 template <int W2, int MODE>
@@ -146,8 +178,9 @@ cudaError_t c2r_pair_t(const CUtensorMap* qmap, float* out, unsigned* peak, cons
     if (e != cudaSuccess) return e;
     const long long units = (long long)((out_rows + C::RPB - 1) / C::RPB) * ntemplates;
     const int grid = (int)(units < cap ? units : cap);
-    return launch_pdl(kernel, dim3(grid), C::THREADS, P::SMEM, s, *qmap, out, peak, tw, out_rows,
-                      out_cols, out_pitch, ntemplates, out_tstride, status);
+    return launch_pdl(kernel, dim3(grid), C::THREADS, P::SMEM, s, *qmap, out, peak,
+                      g_tt[device].col, out_rows, out_cols, out_pitch, ntemplates, out_tstride,
+                      status);
 }
 
 // The pruned starts (nz = 1, 2) are instantiated for sizes >= 1024, where
@@ -158,6 +191,21 @@ constexpr bool kPruned = ZF_SIZE >= 1024;
 
 #define ZF_CAT2(a, b) a##b
 #define ZF_CAT(a, b) ZF_CAT2(a, b)
+
+cudaError_t ZF_CAT(init_thread_twiddles_, ZF_SIZE)(const float2* roots, int device) {
+    if (device < 0 || device >= kMaxDevices) return cudaErrorInvalidDevice;
+    k_fill_thread_twiddles<<<3, kTtThreads>>>(roots);
+    cudaError_t e = cudaGetLastError();
+    void* p = nullptr;
+    if (e == cudaSuccess) e = cudaGetSymbolAddress(&p, g_tt_row);
+    if (e != cudaSuccess) return e;
+    g_tt[device].row = static_cast<const float4*>(p);
+    if ((e = cudaGetSymbolAddress(&p, g_tt_col)) != cudaSuccess) return e;
+    g_tt[device].col = static_cast<const float4*>(p);
+    if ((e = cudaGetSymbolAddress(&p, g_tt_rev)) != cudaSuccess) return e;
+    g_tt[device].rev = static_cast<const float4*>(p);
+    return cudaSuccess;
+}
 
 cudaError_t ZF_CAT(launch_row_r2c_, ZF_SIZE)(const float* tmpl, float2* R, const float2* tw, int h,
                                              int w, int r_pitch, long long r_tstride,

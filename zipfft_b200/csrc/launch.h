@@ -9,6 +9,10 @@
 
 namespace zf {
 
+// init_thread_twiddles_<n>: fills the per-thread twiddle tables of size n's
+// kernels from the n-point root table on the current device (on the legacy
+// default stream; the caller synchronizes) and records their addresses.  Every
+// launcher of that size and device needs it first.
 // Row r2c of `ntemplates` templates (h x w each, consecutive in tmpl) of a
 // W-column image: R of template j at R + j * r_tstride, element (kx, n) at
 // kx * r_pitch + n.  nz: 1 or 2 when the template row fits the first 1 or 2
@@ -28,6 +32,7 @@ namespace zf {
 // arg == nullptr and peak != nullptr, the map's largest value is also folded
 // into *peak as an ordered_key (atomicMax).
 #define ZF_DECL(N)                                                                              \
+    cudaError_t init_thread_twiddles_##N(const float2* roots, int device);                      \
     cudaError_t launch_row_r2c_##N(const float* tmpl, float2* R, const float2* tw, int h, int w, \
                                    int r_pitch, long long r_tstride, int ntemplates, float scale, \
                                    int nz, int device, cudaStream_t s);                          \

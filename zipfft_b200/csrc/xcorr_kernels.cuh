@@ -104,7 +104,8 @@ struct RowLoader {
 template <int W2, int NZ>
 __global__ void __launch_bounds__(R2cCfg<W2>::THREADS)
     k_row_r2c(const float* __restrict__ tmpl, float2* __restrict__ R, const float2* __restrict__ twW,
-              int h, int w, int r_pitch, long long r_tstride, int ntemplates, float scale) {
+              const float4* __restrict__ twt, int h, int w, int r_pitch, long long r_tstride,
+              int ntemplates, float scale) {
     using C = R2cCfg<W2>;
     using F = Stockham<W2, C::T, false, false>;
     static_assert(F::S >= 2, "row FFT needs at least two stages");
@@ -117,7 +118,7 @@ __global__ void __launch_bounds__(R2cCfg<W2>::THREADS)
 
     pdl_launch_dependents();
     typename F::Twiddles tw;
-    F::template load_twiddles<2 * W2>(tw, twW, t);
+    F::load_thread_twiddles(tw, twt, t);
     // R may still be read by the previous kernel of the stream.
     pdl_wait_prerequisites();
 
@@ -208,9 +209,10 @@ struct ColCfg {
 template <int H, bool CONJ, int NZ>
 __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
     k_col_fused(float2* __restrict__ Q, const float2* __restrict__ R, int r_pitch,
-                const float2* __restrict__ spec, const float2* __restrict__ twH, int h, int W2,
-                int store_rows, int discard_r, int ntemplates, long long q_tstride,
-                long long r_tstride, int* __restrict__ status) {
+                const float2* __restrict__ spec, const float4* __restrict__ twt,
+                const float4* __restrict__ twt_rev, int h, int W2, int store_rows, int discard_r,
+                int ntemplates, long long q_tstride, long long r_tstride,
+                int* __restrict__ status) {
     using C = ColCfg<H, NZ>;
     using F = Stockham<H, C::T, false, false>;
     using I = Stockham<H, C::T, true, true>;
@@ -240,13 +242,10 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
 
     pdl_launch_dependents();
     typename F::Twiddles twf;
-    F::template load_twiddles<H>(twf, twH, t);
+    F::load_thread_twiddles(twf, twt, t);
     constexpr bool kShare = plan_palindrome(H);
     typename I::Twiddles twi_own;
-    if constexpr (!kShare) I::template load_twiddles<H>(twi_own, twH, t);
-    // R comes from the previous kernel; Q may still be read by the one before.
-    pdl_wait_prerequisites();
-
+    if constexpr (!kShare) I::load_thread_twiddles(twi_own, twt_rev, t);
     const uint32_t r_bytes = (uint32_t)round_up(h, 2) * 8u;
     // Units (template, column group): ntemplates templates of W2 + 1 virtual
     // columns each, template j's Q and R at Q + j q_tstride, R + j r_tstride.
@@ -261,10 +260,12 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
     const uint64_t pol_spec = l2_evict_normal();
     const uint64_t pol_keep = l2_evict_last();
 
-    // Thread 0 fetches the spectrum and template columns of unit u into buffer b.
-    auto issue = [&](int b, int u) {
+    // Thread 0 fetches the spectrum and template columns of unit u into
+    // buffer b: the spectrum part (which no kernel writes) and the template
+    // part (written by the row kernel before this one) separately, both
+    // completing on the buffer's barrier.
+    auto issue_spec = [&](int b, int u) {
         const int tj = u / cgroups, vc0 = (u - tj * cgroups) * C::FPB;
-        const float2* Rj = R + tj * r_tstride;
         uint32_t bytes = 0;
         for (int j = 0; j < C::FPB; ++j)
             if (vc0 + j <= W2) bytes += H * 8u + r_bytes;
@@ -274,11 +275,29 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
             if (vc > W2) break;
             tma_load_1d(sbase + (b * C::FPB + j) * C::SB, spec + (size_t)vc * H, H * 8u, &mbar[b],
                         pol_spec);
+        }
+    };
+    auto issue_r = [&](int b, int u) {
+        const int tj = u / cgroups, vc0 = (u - tj * cgroups) * C::FPB;
+        const float2* Rj = R + tj * r_tstride;
+        for (int j = 0; j < C::FPB; ++j) {
+            const int vc = vc0 + j;
+            if (vc > W2) break;
             const int rc = vc == W2 ? 0 : vc;
             tma_load_1d(rbase + (b * C::FPB + j) * C::RB, Rj + (size_t)rc * r_pitch, r_bytes,
                         &mbar[b], pol_stream);
         }
     };
+    auto issue = [&](int b, int u) {
+        issue_spec(b, u);
+        issue_r(b, u);
+    };
+
+    // The first unit's spectrum columns do not depend on the previous kernel:
+    // their copy overlaps its tail.  R comes from the previous kernel; Q may
+    // still be read by the one before.
+    if (tid == 0 && (int)blockIdx.x < units) issue_spec(0, blockIdx.x);
+    pdl_wait_prerequisites();
 
     // Double buffering: thread 0 refills the other pair of buffers with the
     // next group once the block is past this group's barrier (their last
@@ -287,7 +306,7 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
     // store.  (Refilling before the wait, or filling both buffers up front,
     // measured slower.)
     int u = blockIdx.x;
-    if (tid == 0 && u < units) issue(0, u);
+    if (tid == 0 && u < units) issue_r(0, u);
     for (int it = 0; u < units; ++it, u += gridDim.x) {
         const int b = it & 1;
         const uint32_t parity = (it >> 1) & 1;
@@ -299,6 +318,9 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
         if (__syncthreads_or(!ok)) {
             if (tid == 0) {
                 atomicExch(status, kStatusTimeout);
+                // The late copy may still land (the next one was not issued):
+                // wait for it, bounded, before the block's memory is released.
+                mbar_wait_bounded(&mbar[b], parity);
                 bulk_wait_all();
             }
             return;
@@ -461,7 +483,7 @@ struct ColFwdCfg {
 
 template <int H>
 __global__ void __launch_bounds__(ColFwdCfg<H>::THREADS, ColFwdCfg<H>::MINB)
-    k_col_fwd(float2* __restrict__ spec, const float2* __restrict__ twH, int W2,
+    k_col_fwd(float2* __restrict__ spec, const float4* __restrict__ twt, int W2,
               int* __restrict__ status) {
     using C = ColFwdCfg<H>;
     using F = Stockham<H, C::T, false, false>;
@@ -487,7 +509,7 @@ __global__ void __launch_bounds__(ColFwdCfg<H>::THREADS, ColFwdCfg<H>::MINB)
 
     pdl_launch_dependents();
     typename F::Twiddles tw;
-    F::template load_twiddles<H>(tw, twH, t);
+    F::load_thread_twiddles(tw, twt, t);
     // The row pass over the image wrote the columns.
     pdl_wait_prerequisites();
 
@@ -526,7 +548,16 @@ __global__ void __launch_bounds__(ColFwdCfg<H>::THREADS, ColFwdCfg<H>::MINB)
         const float2* col = cbase + (b * C::FPB + g) * C::CB;
         float2 v[F::MAXE];
         auto ld = [&](int i) { return col[i]; };
-        F::template run_loader<0>(v, ld, xbuf, tw, t);
+        // With one column per block the column index is block-uniform: only
+        // the block holding packed column 0 writes the exchange buffer after
+        // the transform, so only it needs the barrier after the last
+        // exchange (every block's next write of the buffer is behind the
+        // loop-top barrier).  Blocks of several columns keep the barrier.
+        constexpr bool kUniform = C::FPB == 1;
+        F::template run_loader<0, !kUniform>(v, ld, xbuf, tw, t);
+        if constexpr (kUniform) {
+            if (kx == 0) __syncthreads();
+        }
 
         // Frequency k = bb + r * NBL sits in v[q * RL + r].
         if (kx == 0) {
@@ -549,7 +580,7 @@ __global__ void __launch_bounds__(ColFwdCfg<H>::THREADS, ColFwdCfg<H>::MINB)
                 }
             }
         }
-        __syncthreads();
+        if (!kUniform || kx == 0) __syncthreads();  // block-uniform
         if (kx == 0) {  // split the packed column (its reads ended at the barrier above)
             float2* s0 = spec;
             float2* sn = spec + (size_t)W2 * H;
@@ -609,15 +640,31 @@ constexpr int kRunningMax = 1;  // fold it into a running per-pixel max / argmax
 constexpr int kRunningStats = 2;  // ... and into per-pixel sum and sum of squares
 constexpr int kStorePeak = 3;  // write the map and fold its maximum into *peak
 
+// Maximum that returns NaN when either argument is NaN (as torch.amax does),
+// unlike fmaxf.  fold_warp_peak gives every NaN (of either sign: arithmetic
+// on a NaN input may set its sign bit) the largest key, so it survives
+// atomicMax and converts back to a NaN peak.
+#if defined(__CUDA_ARCH__)
+ZF_DEV float fmax_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+#else
+inline float fmax_nan(float a, float b) { return (a != a || b != b) ? a + b : (a > b ? a : b); }
+#endif
+
 // kStorePeak: each warp keeps its largest stored value over the row groups of
 // one template and folds it into that template's key (one atomic per warp)
 // when its block moves on to another template or ends.  An atomic per warp
 // and group put ~16k atomics on one address per 4096-row template, which
-// serialised in L2.  Every lane of the warp must call this.
+// serialised in L2.  Every lane of the warp must call this.  A block that
+// gives up on a bounded wait folds what it has before it returns; the peaks
+// of such a call are incomplete (the device status word reports it).
 ZF_DEV void fold_warp_peak(float v, unsigned* key) {
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    if ((threadIdx.x & 31) == 0) atomicMax(key, ordered_key(v));
+    for (int o = 16; o > 0; o >>= 1) v = fmax_nan(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if ((threadIdx.x & 31) == 0) atomicMax(key, v != v ? 0xFFFFFFFFu : ordered_key(v));
 }
 
 // MODE kStoreMap: out[y][x] = correlation.  MODE kRunningMax: out is the
@@ -632,9 +679,10 @@ template <int W2, int MODE>
 __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     k_row_c2r(const __grid_constant__ CUtensorMap qmap, float* __restrict__ out,
               int* __restrict__ arg, float* __restrict__ sum, float* __restrict__ sumsq,
-              unsigned* __restrict__ peak, const float2* __restrict__ twW, int out_rows,
-              int out_cols, int out_pitch, int tindex, int reset, int ntemplates,
-              long long out_tstride, int* __restrict__ status) {
+              unsigned* __restrict__ peak, const float2* __restrict__ twW,
+              const float4* __restrict__ twt, int out_rows, int out_cols, int out_pitch,
+              int tindex, int reset, int ntemplates, long long out_tstride,
+              int* __restrict__ status) {
     using C = C2rCfg<W2>;
     using I = Stockham<W2, C::T, true, false>;
     static_assert(I::S >= 2, "row FFT needs at least two stages");
@@ -658,7 +706,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
 
     pdl_launch_dependents();
     typename I::Twiddles tw;
-    I::template load_twiddles<2 * W2>(tw, twW, t);
+    I::load_thread_twiddles(tw, twt, t);
     // Pre-pass twiddles w_W^-k for k = bb + r NB0: w^-bb (per butterfly, from
     // the table) times w_W^-(r NB0) = w_{2 R0}^-r (compile-time roots).
     float2 wpre[I::bpt(0)];
@@ -734,7 +782,10 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
             if (tid == 0 && more) prefetch_maps(u + gridDim.x);
         }
         const bool ok = mbar_wait_bounded(&mbar[b], parity);
-        if (__syncthreads_or(!ok)) {
+        if (__syncthreads_or(!ok)) {  // block-uniform: every lane folds its warp
+            if constexpr (MODE == kStorePeak) {
+                if (pk_t >= 0) fold_warp_peak(pk_run, peak + pk_t);
+            }
             if (tid == 0) {
                 atomicExch(status, kStatusTimeout);
                 if (more) mbar_wait_bounded(&mbar[b ^ 1], ((it + 1) >> 1) & 1);
@@ -755,11 +806,20 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                     const int k = bb + r * NB0;
                     const float2 A = qt[k * C::RPB];
                     const float2 B = qt[((W2 - k) % W2) * C::RPB];
-                    const float2 E2 = c_make(A.x + B.x, A.y - B.y);  // A + conj B
-                    const float2 D = c_make(A.x - B.x, A.y + B.y);   // A - conj B
-                    // w^-k D = (w^-bb D) w_{2 R0}^-r
-                    const float2 P = c_mul_w<2 * R0 - r, 2 * R0, false>(c_mul(D, wb));
-                    float2 z = c_make(E2.x - P.y, E2.y + P.x);         // E2 + i P
+                    const float2 E2 = px_fma(B, c_make(1.f, -1.f), A);  // A + conj B
+                    const float2 D = px_fma(B, c_make(-1.f, 1.f), A);   // A - conj B
+                    // z = E2 + i P with P = w^-k D = (w^-bb D) w_{2 R0}^-r; the
+                    // constant root is folded into the sum when it is +-i.
+                    const float2 Pb = c_mul(D, wb);
+                    float2 z;
+                    if constexpr (is_quarter_turn<2 * R0 - r, 2 * R0, false>()) {
+                        // i (+-i) Pb = -+Pb
+                        z = quarter_turn_inv<2 * R0 - r, 2 * R0, false>() ? c_sub(E2, Pb)
+                                                                          : c_add(E2, Pb);
+                    } else {
+                        const float2 P = c_mul_w<2 * R0 - r, 2 * R0, false>(Pb);
+                        z = px_fma(c_swap(P), c_make(-1.f, 1.f), E2);  // E2 + i P
+                    }
                     if (r == 0 && bb == 0) z = c_make(A.x + A.y, A.x - A.y);  // packed (X0, X_W2)
                     v[q * R0 + r] = z;
                 });
@@ -794,15 +854,15 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                                 const float2 z = v[q * RL + r];
                                 if (FULL || (rv && 2 * m + 1 < out_cols)) {
                                     st_hint(reinterpret_cast<float2*>(orow) + m, z, pol_stream);
-                                    if constexpr (MODE == kStorePeak) pk = fmaxf(pk, fmaxf(z.x, z.y));
+                                    if constexpr (MODE == kStorePeak) pk = fmax_nan(pk, fmax_nan(z.x, z.y));
                                 } else {
                                     if (2 * m < out_cols) {
                                         st_hint(orow + 2 * m, z.x, pol_stream);
-                                        if constexpr (MODE == kStorePeak) pk = fmaxf(pk, z.x);
+                                        if constexpr (MODE == kStorePeak) pk = fmax_nan(pk, z.x);
                                     }
                                     if (2 * m + 1 < out_cols) {
                                         st_hint(orow + 2 * m + 1, z.y, pol_stream);
-                                        if constexpr (MODE == kStorePeak) pk = fmaxf(pk, z.y);
+                                        if constexpr (MODE == kStorePeak) pk = fmax_nan(pk, z.y);
                                     }
                                 }
                             }
@@ -927,7 +987,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
             }
         }
         // Rows past the end contribute -inf.
-        if constexpr (MODE == kStorePeak) pk_run = fmaxf(pk_run, pk);
+        if constexpr (MODE == kStorePeak) pk_run = fmax_nan(pk_run, pk);
     }
     if constexpr (MODE == kStorePeak) {
         if (pk_t >= 0) fold_warp_peak(pk_run, peak + pk_t);
@@ -959,7 +1019,7 @@ struct C2rPairCfg {
 template <int W2, int MODE>
 __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     k_row_c2r_pair(const __grid_constant__ CUtensorMap qmap, float* __restrict__ out,
-                   unsigned* __restrict__ peak, const float2* __restrict__ twW, int out_rows,
+                   unsigned* __restrict__ peak, const float4* __restrict__ twt, int out_rows,
                    int out_cols, int out_pitch, int ntemplates, long long out_tstride,
                    int* __restrict__ status) {
     static_assert(MODE == kStoreMap || MODE == kStorePeak, "map epilogues only");
@@ -987,7 +1047,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
 
     pdl_launch_dependents();
     typename I::Twiddles tw;
-    I::template load_twiddles<W>(tw, twW, t);
+    I::load_thread_twiddles(tw, twt, t);
     // Q comes from the previous kernel.
     pdl_wait_prerequisites();
 
@@ -1023,7 +1083,10 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
         const bool more = u + (int)gridDim.x < units;
         if (tid == 0 && more) issue(b ^ 1, u + gridDim.x);
         const bool ok = mbar_wait_bounded(&mbar[b], parity);
-        if (__syncthreads_or(!ok)) {
+        if (__syncthreads_or(!ok)) {  // block-uniform: every lane folds its warp
+            if constexpr (MODE == kStorePeak) {
+                if (pk_t >= 0) fold_warp_peak(pk_run, peak + pk_t);
+            }
             if (tid == 0) {
                 atomicExch(status, kStatusTimeout);
                 if (more) mbar_wait_bounded(&mbar[b ^ 1], ((it + 1) >> 1) & 1);
@@ -1089,11 +1152,11 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                         if (FULL || n < out_cols) {
                             if (has0) {
                                 st_hint(row0 + n, z.x, pol_stream);
-                                if constexpr (MODE == kStorePeak) pk = fmaxf(pk, z.x);
+                                if constexpr (MODE == kStorePeak) pk = fmax_nan(pk, z.x);
                             }
                             if (has1) {
                                 st_hint(row1 + n, z.y, pol_stream);
-                                if constexpr (MODE == kStorePeak) pk = fmaxf(pk, z.y);
+                                if constexpr (MODE == kStorePeak) pk = fmax_nan(pk, z.y);
                             }
                         }
                     }
@@ -1104,7 +1167,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
             emit(std::true_type{});
         else
             emit(std::false_type{});
-        if constexpr (MODE == kStorePeak) pk_run = fmaxf(pk_run, pk);
+        if constexpr (MODE == kStorePeak) pk_run = fmax_nan(pk_run, pk);
     }
     if constexpr (MODE == kStorePeak) {
         if (pk_t >= 0) fold_warp_peak(pk_run, peak + pk_t);

@@ -36,8 +36,15 @@ def _check(cond: bool, msg: str) -> None:
 
 
 def _validate(input: torch.Tensor, fft_workspace: torch.Tensor, conv_data: torch.Tensor,
-              output: torch.Tensor, fft_size_y: int, fft_size_x: int):
-    """Checks of real_conv_2d_binding.cu:196-263, same order and messages."""
+              output: torch.Tensor, fft_size_y: int, fft_size_x: int, *,
+              output_is_shape_stand_in: bool = False):
+    """Checks of real_conv_2d_binding.cu:196-263, same order and messages.
+
+    output_is_shape_stand_in: `output` is an expanded view that only carries
+    the per-template map shape (corr_max, whose kernels write the running maps
+    instead); its contiguity is not checked.  Every caller whose `output`
+    receives the maps leaves this False, so an expanded or overlapping output
+    (stride 0 over the batch) is rejected before anything launches."""
     _check(input.device.type == "cuda", "Input tensor must be on CUDA device")
     _check(fft_workspace.device.type == "cuda", "FFT workspace tensor must be on CUDA device")
     _check(conv_data.device.type == "cuda", "Convolution data tensor must be on CUDA device")
@@ -94,8 +101,7 @@ def _validate(input: torch.Tensor, fft_workspace: torch.Tensor, conv_data: torch
                                         "batch size")
     for name, t in (("Input", input), ("FFT workspace", fft_workspace),
                     ("Convolution data", conv_data), ("Output", output)):
-        # (an expanded view stands in for corr_max's per-template output)
-        if t is output and output.dim() == 3 and output.stride(0) == 0:
+        if t is output and output_is_shape_stand_in:
             continue
         _check(t.is_contiguous(), f"{name} tensor must be contiguous")
     return batch, sy, sx, output.size(-2), output.size(-1)
@@ -194,7 +200,7 @@ def corr_max(input: torch.Tensor, fft_workspace: torch.Tensor, conv_data: torch.
     # the per-template output.
     batch, sy, sx, oy, ox = _validate(input, fft_workspace, conv_data,
                                       max_map.expand(*lead, *max_map.shape), int(fft_size_y),
-                                      int(fft_size_x))
+                                      int(fft_size_x), output_is_shape_stand_in=True)
     lib = _lib.load()
     device = input.device.index if input.device.index is not None else torch.cuda.current_device()
     stream = torch.cuda.current_stream(device).cuda_stream
