@@ -103,9 +103,12 @@ ZFFT_API int zfft_padded_real_corr_2d_max(const float* input, int batch, int sig
 
 /* zfft_padded_real_corr_2d_max that also accumulates, per pixel, the sum and
  * the sum of squares of the correlations over the templates (float32 maps of
- * the same shape; reset overwrites them with the first template's values):
- * the statistics 2D template matching normalises its scores with.  No
- * counterpart in the reference (README.md:24 motivates the use). */
+ * the same shape): the statistics 2D template matching normalises its scores
+ * with.  reset: 0 folds every template into all four maps; 1 lets the first
+ * template overwrite all four; 2 lets it overwrite the two sum maps only (the
+ * maximum and argmax keep folding), so that a long search can sum each batch
+ * in float32 and add the batches up at higher precision.  No counterpart in
+ * the reference (README.md:24 motivates the use). */
 ZFFT_API int zfft_padded_real_corr_2d_max_stats(const float* input, int batch, int signal_y,
                                                 int signal_x, void* fft_workspace,
                                                 size_t fft_workspace_bytes, const void* conv_data,

@@ -628,6 +628,10 @@ int main(int argc, char** argv) {
     const int group = max_mode ? 0 : (hd[13] & 0xFFFF);  // >= 2: batched groups
     const bool poison = (hd[13] >> 16) & 1;              // workspace starts as NaN
     emu_defer_loads = (hd[13] >> 17) & 1;                // TMA loads land at the wait
+    // max_mode 2 with bit 18: every second template starts a new "batch"
+    // whose first template overwrites only the sum maps (reset kResetSums),
+    // as the search's per-batch partial sums do; the maximum keeps running.
+    const bool sum_batches = (hd[13] >> 18) & 1;
     const int W2 = W / 2;
     std::vector<float> tm((size_t)B * sy * sx);
     std::vector<float2> spec((size_t)(W2 + 1) * H);
@@ -687,7 +691,8 @@ int main(int argc, char** argv) {
             col(H, conj, nz_col, Q, Rt, rp, spec.data(), twH.data(), sy, W2, oy, cap);
             if (max_mode)
                 c2r(W, Q, H, out.data(), arg.data(), sum_p, sumsq_p, nullptr, twW.data(), oy, ox, t,
-                    t == 0, cap);
+                    t == 0 ? zf::kResetMax : ((sum_batches && t % 2 == 0) ? zf::kResetSums : 0),
+                    cap);
             else
                 c2r(W, Q, H, out.data() + (size_t)t * oy * ox, nullptr, nullptr, nullptr,
                     peaks_mode ? peak_keys.data() + t : nullptr, twW.data(), oy, ox, 0, 0, cap);

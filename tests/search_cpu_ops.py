@@ -19,14 +19,15 @@ def corr_max(batch, workspace, conv_data, max_map, arg_map, H, W, base, reset, s
     am = arg_map.numpy()
     for t in range(res.shape[0]):
         v = res[t].astype(np.float32)
-        first = reset and t == 0
+        first = reset == 1 and t == 0        # RESET_ALL: every map
+        first_sums = reset in (1, 2) and t == 0  # RESET_SUMS: the sum maps only
         upd = np.ones_like(mx, bool) if first else (v > mx)
         mx[upd] = v[upd]
         am[upd] = base + t
-        if sum_map is not None:  # float32 accumulation, as on the GPU
+        if sum_map is not None:  # float32 accumulation within the call, as on the GPU
             s, q = sum_map.numpy(), sumsq_map.numpy()
-            s[...] = v if first else s + v
-            q[...] = v * v if first else q + v * v
+            s[...] = v if first_sums else s + v
+            q[...] = v * v if first_sums else q + v * v
 
 
 def pack(max_map, arg_map):

@@ -51,7 +51,7 @@ def nz_of(n, length):
 
 
 def run_emu(exe, tmp_path, B, sy, sx, H, W, conj, full, nz_col=None, nz_row=None, seed=0,
-            chunk=0, max_mode=False, group=0, poison=False, defer=False):
+            chunk=0, max_mode=False, group=0, poison=False, defer=False, sum_batches=False):
     rng = np.random.default_rng(seed)
     img = rng.standard_normal((H, W)).astype(np.float32)
     tm = rng.standard_normal((B, sy, sx)).astype(np.float32)
@@ -62,7 +62,8 @@ def run_emu(exe, tmp_path, B, sy, sx, H, W, conj, full, nz_col=None, nz_row=None
     fin, fout = str(tmp_path / "in.bin"), str(tmp_path / "out.bin")
     with open(fin, "wb") as f:
         np.array([B, sy, sx, H, W, oy, ox, int(conj), 3, nz_col, nz_row, chunk, int(max_mode),
-                  group + (1 << 16 if poison else 0) + (1 << 17 if defer else 0)],
+                  group + (1 << 16 if poison else 0) + (1 << 17 if defer else 0)
+                  + (1 << 18 if sum_batches else 0)],
                  np.int32).tofile(f)
         tm.tofile(f)
         spec.tofile(f)
@@ -276,3 +277,17 @@ def test_emulated_kernels_with_late_tma_arrival(emu, tmp_path, case):
     assert O.max_abs_over_peak(ref, out) < 1e-5
     if max_mode == 3:
         assert np.array_equal(got[1], out.reshape(B, -1).max(axis=1))
+
+
+def test_emulated_stats_batches_restart_sums_keep_max(emu, tmp_path):
+    """reset = kResetSums on a batch's first template (the search's per-batch
+    partial sums): the sum maps restart there, the maximum and argmax keep
+    folding every template."""
+    B = 5
+    (mx, am, sm, sq), ref = run_emu(emu, tmp_path, B, 12, 9, 64, 128, True, True,
+                                    max_mode=2, sum_batches=True)
+    tol = 1e-5 * np.abs(ref).max()
+    assert np.allclose(mx, ref.max(axis=0), rtol=0, atol=tol)
+    last = ref[4:]  # templates 0-1, 2-3 and 4 form the batches
+    assert np.allclose(sm, last.sum(axis=0), rtol=0, atol=tol)
+    assert np.allclose(sq, (last ** 2).sum(axis=0), rtol=0, atol=tol * np.abs(ref).max())

@@ -99,7 +99,7 @@ def test_two_rank_search_matches_single_process(tmp_path, dup):
         am = np.load(tmp_path / f"arg{r}.npy")
         assert np.array_equal(mx, ref_max)
         assert np.array_equal(am, ref_arg)  # ties (dup) keep the lower index, 1 not 4
-        # per-rank float32 partial sums, summed by the SUM all-reduce
+        # per-batch float32 partial sums added in float64, then the SUM all-reduce
         assert O.rel_l2(res.sum(axis=0), np.load(tmp_path / f"sum{r}.npy")) < 1e-6
         assert O.rel_l2((res ** 2).sum(axis=0), np.load(tmp_path / f"sumsq{r}.npy")) < 1e-6
     assert np.array_equal(np.load(tmp_path / "sum0.npy"), np.load(tmp_path / "sum1.npy"))

@@ -91,6 +91,35 @@ def test_corr_max_stats_match_oracle(B, h, w, H, W, full):
     assert torch.equal(mx, mx2) and torch.equal(am, am2)
 
 
+def test_search_stats_over_1024_templates_match_float64_sums():
+    """stats=True over 1024 templates in 4 batches of 256: the kernels sum each
+    batch in float32 and the search adds the batches in float64, so the
+    per-pixel sums stay within the batch's rounding of the oracle's float64
+    sums (naive float32 accumulation over all 1024 would not)."""
+    from zipfft_b200.search import template_search
+
+    H = W = 256
+    N, h = 1024, 16
+    _, tm, spec = make_inputs(N, h, h, H, W, seed=31)
+    dev = torch.device("cuda", 0)
+    mx, am, sm, sq = template_search(tm, spec.to(dev), H, W, batch_size=256, full=True,
+                                     stats=True)
+    torch.cuda.synchronize()
+    assert sm.dtype == torch.float64 and sq.dtype == torch.float64
+    ref_s = np.zeros((H, W))
+    ref_q = np.zeros((H, W))
+    ref_m = np.full((H, W), -np.inf)
+    for b0 in range(0, N, 128):
+        ref = O.padded_corr2d_f64(tm[b0:b0 + 128].numpy(), spec.numpy(), H, W, True, True)
+        ref_s += ref.sum(axis=0)
+        ref_q += (ref ** 2).sum(axis=0)
+        ref_m = np.maximum(ref_m, ref.max(axis=0))
+    scale = np.sqrt(ref_q.max())
+    assert np.abs(sm.cpu().numpy() - ref_s).max() / scale < 1e-5
+    assert O.rel_l2(ref_q, sq.cpu().numpy()) < 5e-6
+    assert O.rel_l2(ref_m, mx.cpu().numpy()) < 5e-6
+
+
 def test_corr_max_stats_argument_errors():
     import zipfft
 

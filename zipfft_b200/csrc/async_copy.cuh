@@ -28,6 +28,9 @@ namespace zf {
 
 // Device status codes written by kernels (same values as the C ABI's).
 constexpr int kStatusTimeout = 4;
+// Bits of the running-map epilogues' `reset` argument (set by the C ABI).
+constexpr int kResetMax = 1;   // overwrite every map (max, argmax, sums)
+constexpr int kResetSums = 2;  // overwrite the sum maps only
 // ~1 s at 2 GHz: far beyond any legitimate copy latency.
 constexpr long long kWaitLimitCycles = 2000000000LL;
 

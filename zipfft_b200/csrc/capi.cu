@@ -293,12 +293,13 @@ const int kConfigs[][6] = {
 // One call of the correlation path.  arg == nullptr: output holds `batch`
 // maps of oy x ox.  Otherwise output / arg are the running max / argmax maps
 // (oy x ox) that every template folds into, template t with index
-// tindex_base + t; reset: the first template overwrites them.  With sum (and
+// tindex_base + t; reset (zf::kResetMax / kResetSums bits): the first
+// template overwrites every map / only the sum maps.  With sum (and
 // sumsq) also given, every template is added to those maps as well.  With
 // peaks (maps mode only), peaks[t] receives the largest value of map t.
 int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes,
         const void* conv_data, float* output, int oy, int ox, int H, int W, bool conj,
-        int device, void* stream, int* arg = nullptr, int tindex_base = 0, bool reset = false,
+        int device, void* stream, int* arg = nullptr, int tindex_base = 0, int reset = 0,
         float* sum = nullptr, float* sumsq = nullptr, float* peaks = nullptr) {
     g_last_error.clear();
     if (batch < 0) return fail(ZFFT_ERROR_INVALID_VALUE, "batch must be >= 0. Got %d.", batch);
@@ -471,7 +472,7 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
             m = timer_mark(s);
             if (arg)
                 e = c2r(&qmap, output, arg, sum, sumsq, nullptr, twW, oy, ox, ox, tindex_base + t,
-                        (reset && t == 0) ? 1 : 0, 1, 0, status, device, s);
+                        t == 0 ? reset : 0, 1, 0, status, device, s);
             else
                 e = c2r(&qmap, output + (size_t)t * oy * ox, nullptr, nullptr, nullptr,
                         peak_keys ? peak_keys + t : nullptr, twW, oy, ox, ox, 0, 0, 1, 0, status,
@@ -698,7 +699,8 @@ int zfft_padded_real_corr_2d_max(const float* input, int batch, int signal_y, in
         return fail(ZFFT_ERROR_INVALID_VALUE, "template indices must lie in [0, 2^31 - 1)");
     return run(input, batch, signal_y, signal_x, fft_workspace, fft_workspace_bytes, conv_data,
                max_map, output_y, output_x, fft_size_y, fft_size_x, true, device, stream,
-               reinterpret_cast<int*>(arg_map), template_index_base, reset != 0);
+               reinterpret_cast<int*>(arg_map), template_index_base,
+               reset != 0 ? zf::kResetMax : 0);
 }
 
 int zfft_padded_real_corr_2d_peaks(const float* input, int batch, int signal_y, int signal_x,
@@ -723,9 +725,14 @@ int zfft_padded_real_corr_2d_max_stats(const float* input, int batch, int signal
         return fail(ZFFT_ERROR_INVALID_VALUE, "null argmax, sum or sum-of-squares map");
     if (template_index_base < 0 || (long long)template_index_base + batch > 0x7FFFFFFFLL)
         return fail(ZFFT_ERROR_INVALID_VALUE, "template indices must lie in [0, 2^31 - 1)");
+    if (reset < 0 || reset > 2)
+        return fail(ZFFT_ERROR_INVALID_VALUE,
+                    "reset must be 0 (fold), 1 (overwrite every map) or 2 (overwrite the sum "
+                    "maps only). Got %d.", reset);
     return run(input, batch, signal_y, signal_x, fft_workspace, fft_workspace_bytes, conv_data,
                max_map, output_y, output_x, fft_size_y, fft_size_x, true, device, stream,
-               reinterpret_cast<int*>(arg_map), template_index_base, reset != 0, sum_map,
+               reinterpret_cast<int*>(arg_map), template_index_base,
+               reset == 1 ? zf::kResetMax : (reset == 2 ? zf::kResetSums : 0), sum_map,
                sumsq_map);
 }
 

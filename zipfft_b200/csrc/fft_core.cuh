@@ -89,15 +89,15 @@ constexpr double cx_sin2pi(long m, long n) {
 // ---------------------------------------------------------------------------
 // Complex helpers (float2 = {re, im})
 //
-// Sums, differences and products by constants run as packed f32x2
-// instructions on the device (FADD2 / FMUL2 / FFMA2: one instruction for both
-// lanes; an operand may broadcast or swap the halves of its register pair and
-// be negated at no cost, measured with ncu on sm_100a).  The packed forms give
-// the FP32 pipe the same work (it retires 128 lanes per clock per SM either
-// way) in half the issue slots.  A product of two variable complex values
-// needs a different sign in each lane, which no operand modifier provides, so
-// c_mul and friends stay scalar (two FMUL + two FFMA).  Host compilation (the
-// CPU test harness) computes the same lanes with scalar IEEE operations.
+// The butterflies below are written with lane-wise helpers (px_*) and fold
+// every quarter turn (+-i) into a sum or difference (c_add_rot / c_sub_rot),
+// so no rotation costs an instruction of its own.  The helpers are scalar
+// FP32 operations.  The packed FADD2 / FMUL2 / FFMA2 instructions of sm_100a
+// were measured as well (same FP32 lane throughput, half the issue slots; an
+// operand may broadcast, swap or negate the halves of its register pair at no
+// cost): one B200 ran the 4096^2 / 256^2 step 2.8% slower with them (the
+// inverse row pass 36.0 us against 34.6 us per template, the column pass
+// unchanged).
 // ---------------------------------------------------------------------------
 ZF_HD float2 c_make(float re, float im) {
     float2 r;
@@ -105,18 +105,12 @@ ZF_HD float2 c_make(float re, float im) {
     r.y = im;
     return r;
 }
-#if defined(__CUDA_ARCH__)
 // lane-wise a + b, a * b, a * b + c (round to nearest)
-ZF_DEV float2 px_add(float2 a, float2 b) { return __fadd2_rn(a, b); }
-ZF_DEV float2 px_mul(float2 a, float2 b) { return __fmul2_rn(a, b); }
-ZF_DEV float2 px_fma(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
-#else
 ZF_HD float2 px_add(float2 a, float2 b) { return c_make(a.x + b.x, a.y + b.y); }
 ZF_HD float2 px_mul(float2 a, float2 b) { return c_make(a.x * b.x, a.y * b.y); }
 ZF_HD float2 px_fma(float2 a, float2 b, float2 c) {
     return c_make(fmaf(a.x, b.x, c.x), fmaf(a.y, b.y, c.y));
 }
-#endif
 ZF_HD float2 c_swap(float2 a) { return c_make(a.y, a.x); }
 ZF_HD float2 c_add(float2 a, float2 b) { return px_add(a, b); }
 ZF_HD float2 c_sub(float2 a, float2 b) { return px_add(a, c_make(-b.x, -b.y)); }
@@ -142,7 +136,7 @@ ZF_HD float2 c_rot(float2 a) {
 }
 // a * i
 ZF_HD float2 c_mul_i(float2 a) { return c_make(-a.y, a.x); }
-// t + rot<INV>(d) and t - rot<INV>(d): one packed FMA of the swapped d.
+// t + rot<INV>(d) and t - rot<INV>(d): the swapped d against (+-1, -+1).
 template <bool INV>
 ZF_HD float2 c_add_rot(float2 t, float2 d) {
     return px_fma(c_swap(d), INV ? c_make(-1.f, 1.f) : c_make(1.f, -1.f), t);
@@ -156,16 +150,15 @@ template <bool INV>
 ZF_HD float2 c_add_rot_scaled(float2 t, float2 d, float s) {
     return px_fma(c_swap(d), INV ? c_make(-s, s) : c_make(s, -s), t);
 }
-// a * (wr + i wi) for constants: two packed instructions (the broadcast
-// halves of a against (wr, wi) and (-wi, wr)).
+// a * (wr + i wi) for constants.
 ZF_HD float2 c_mul_const(float2 a, float wr, float wi) {
     return px_fma(c_make(a.x, a.x), c_make(wr, wi), px_mul(c_make(a.y, a.y), c_make(-wi, wr)));
 }
 
 // Multiply by the compile-time root of unity exp(-+2 pi i M / N) (forward sign
-// "-", inverse sign "+").  Exact special cases avoid multiplications.  A
-// quarter turn (+-i) costs an instruction of its own here; the butterflies
-// below fold those into the following sum instead (c_add_rot / c_sub_rot).
+// "-", inverse sign "+").  Exact special cases avoid multiplications; the
+// butterflies below fold quarter turns (+-i) into the following sum instead
+// (c_add_rot / c_sub_rot).
 template <int M, int N, bool INV>
 ZF_HD float2 c_mul_w(float2 a) {
     constexpr int m0 = ((M % N) + N) % N;

@@ -58,6 +58,12 @@ float2* dyn_smem();  // provided by the CPU test harness
 // ragged 20, at the price of n / 240 idle threads in radix-16 stages.
 constexpr int fft_threads(int n) { return n % 15 == 0 ? n / 15 : (n + 15) / 16; }
 constexpr int round_up(int x, int m) { return (x + m - 1) / m * m; }
+// Largest divisor of n that is at most cap.
+constexpr int largest_divisor_upto(int n, int cap) {
+    for (int d = cap; d > 1; --d)
+        if (n % d == 0) return d;
+    return 1;
+}
 constexpr int cmax(int a, int b) { return a > b ? a : b; }
 // Padded exchange buffer length, = 4 (mod 16): buffers of consecutive rows then
 // start 8 banks apart, so the split passes (which walk 4 rows in lockstep)
@@ -640,6 +646,7 @@ constexpr int kRunningMax = 1;  // fold it into a running per-pixel max / argmax
 constexpr int kRunningStats = 2;  // ... and into per-pixel sum and sum of squares
 constexpr int kStorePeak = 3;  // write the map and fold its maximum into *peak
 
+
 // Maximum that returns NaN when either argument is NaN (as torch.amax does),
 // unlike fmaxf.  fold_warp_peak gives every NaN (of either sign: arithmetic
 // on a NaN input may set its sign bit) the largest key, so it survives
@@ -670,11 +677,13 @@ ZF_DEV void fold_warp_peak(float v, unsigned* key) {
 // MODE kStoreMap: out[y][x] = correlation.  MODE kRunningMax: out is the
 // running maximum map and arg the template-index map (same pitch); where the
 // correlation is strictly greater than the stored maximum (or everywhere when
-// `reset`), the maximum becomes the correlation and the index `tindex`.
-// Templates folded in increasing index order therefore keep the lowest index
-// on ties.  MODE kRunningStats: as kRunningMax, and the correlation and its
-// square are also added to the maps sum and sumsq (same pitch; `reset`
-// overwrites them instead).
+// reset & kResetMax), the maximum becomes the correlation and the index
+// `tindex`.  Templates folded in increasing index order therefore keep the
+// lowest index on ties.  MODE kRunningStats: as kRunningMax, and the
+// correlation and its square are also added to the maps sum and sumsq (same
+// pitch; reset & (kResetMax | kResetSums) overwrites them instead, so that a
+// caller can start float32 partial sums per batch and accumulate the batches
+// at higher precision while the maximum keeps running).
 template <int W2, int MODE>
 __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     k_row_c2r(const __grid_constant__ CUtensorMap qmap, float* __restrict__ out,
@@ -876,36 +885,38 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
             } else {
                 int* arow = arg + (size_t)y * out_pitch;
                 const bool rv = aligned8(orow) && aligned8(arow);
-                // All loads of the stored maxima first, then the updates.
-                float2 cur[I::bpt(I::S - 1) * RL];
+                // A chunk of a butterfly's outputs at a time, loads of the
+                // stored values first, then the updates (all of them at once
+                // held too many registers).
+                constexpr int MCH = largest_divisor_upto(RL, 8);
 #pragma unroll
                 for (int q = 0; q < I::bpt(I::S - 1); ++q) {
                     const int bb = t + q * C::T;
+                    if (!(I::even(I::S - 1) || bb < NBL)) continue;
 #pragma unroll
-                    for (int r = 0; r < RL; ++r) {
-                        const int m = bb + r * NBL;
-                        float2 c = c_make(-INFINITY, -INFINITY);
-                        if (!reset && (I::even(I::S - 1) || bb < NBL)) {
-                            if (rv && 2 * m + 1 < out_cols) {
-                                c = reinterpret_cast<const float2*>(orow)[m];
-                            } else {
-                                if (2 * m < out_cols) c.x = orow[2 * m];
-                                if (2 * m + 1 < out_cols) c.y = orow[2 * m + 1];
+                    for (int r0 = 0; r0 < RL; r0 += MCH) {
+                        float2 cur[MCH];
+#pragma unroll
+                        for (int i = 0; i < MCH; ++i) {
+                            const int m = bb + (r0 + i) * NBL;
+                            float2 c = c_make(-INFINITY, -INFINITY);
+                            if (!(reset & kResetMax)) {
+                                if (rv && 2 * m + 1 < out_cols) {
+                                    c = reinterpret_cast<const float2*>(orow)[m];
+                                } else {
+                                    if (2 * m < out_cols) c.x = orow[2 * m];
+                                    if (2 * m + 1 < out_cols) c.y = orow[2 * m + 1];
+                                }
                             }
+                            cur[i] = c;
                         }
-                        cur[q * RL + r] = c;
-                    }
-                }
 #pragma unroll
-                for (int q = 0; q < I::bpt(I::S - 1); ++q) {
-                    const int bb = t + q * C::T;
-                    if (I::even(I::S - 1) || bb < NBL) {
-#pragma unroll
-                        for (int r = 0; r < RL; ++r) {
-                            const int m = bb + r * NBL;
-                            const float2 z = v[q * RL + r];
-                            const float2 c = cur[q * RL + r];
-                            const bool u0 = reset || z.x > c.x, u1 = reset || z.y > c.y;
+                        for (int i = 0; i < MCH; ++i) {
+                            const int m = bb + (r0 + i) * NBL;
+                            const float2 z = v[q * RL + r0 + i];
+                            const float2 c = cur[i];
+                            const bool rmax = (reset & kResetMax) != 0;
+                            const bool u0 = rmax || z.x > c.x, u1 = rmax || z.y > c.y;
                             if (rv && 2 * m + 1 < out_cols) {
                                 if (u0 && u1) {
                                     reinterpret_cast<float2*>(orow)[m] = z;
@@ -932,41 +943,46 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                 }
                 if constexpr (MODE == kRunningStats) {
                     // Per-pixel sum and sum of squares (float accumulation);
-                    // a butterfly's RL values at a time: loads first, then stores.
+                    // a chunk of a butterfly's outputs at a time, loads first.
                     float* srow = sum + (size_t)y * out_pitch;
                     float* qrow = sumsq + (size_t)y * out_pitch;
                     const bool rvs = aligned8(srow) && aligned8(qrow);
+                    const bool fresh = (reset & (kResetMax | kResetSums)) != 0;
+                    constexpr int SCH = largest_divisor_upto(RL, 4);
 #pragma unroll
                     for (int q = 0; q < I::bpt(I::S - 1); ++q) {
                         const int bb = t + q * C::T;
-                        if (I::even(I::S - 1) || bb < NBL) {
-                            float2 s1[RL], s2[RL];
+                        if (!(I::even(I::S - 1) || bb < NBL)) continue;
 #pragma unroll
-                            for (int r = 0; r < RL; ++r) {
-                                const int m = bb + r * NBL;
-                                s1[r] = s2[r] = c_make(0.f, 0.f);
-                                if (!reset) {
+                        for (int r0 = 0; r0 < RL; r0 += SCH) {
+                            float2 s1[SCH], s2[SCH];
+#pragma unroll
+                            for (int i = 0; i < SCH; ++i) {
+                                const int m = bb + (r0 + i) * NBL;
+                                s1[i] = s2[i] = c_make(0.f, 0.f);
+                                if (!fresh) {
                                     if (rvs && 2 * m + 1 < out_cols) {
-                                        s1[r] = reinterpret_cast<const float2*>(srow)[m];
-                                        s2[r] = reinterpret_cast<const float2*>(qrow)[m];
+                                        s1[i] = reinterpret_cast<const float2*>(srow)[m];
+                                        s2[i] = reinterpret_cast<const float2*>(qrow)[m];
                                     } else {
                                         if (2 * m < out_cols) {
-                                            s1[r].x = srow[2 * m];
-                                            s2[r].x = qrow[2 * m];
+                                            s1[i].x = srow[2 * m];
+                                            s2[i].x = qrow[2 * m];
                                         }
                                         if (2 * m + 1 < out_cols) {
-                                            s1[r].y = srow[2 * m + 1];
-                                            s2[r].y = qrow[2 * m + 1];
+                                            s1[i].y = srow[2 * m + 1];
+                                            s2[i].y = qrow[2 * m + 1];
                                         }
                                     }
                                 }
                             }
 #pragma unroll
-                            for (int r = 0; r < RL; ++r) {
-                                const int m = bb + r * NBL;
-                                const float2 z = v[q * RL + r];
-                                const float2 a = c_make(s1[r].x + z.x, s1[r].y + z.y);
-                                const float2 b2 = c_make(fmaf(z.x, z.x, s2[r].x), fmaf(z.y, z.y, s2[r].y));
+                            for (int i = 0; i < SCH; ++i) {
+                                const int m = bb + (r0 + i) * NBL;
+                                const float2 z = v[q * RL + r0 + i];
+                                const float2 a = c_make(s1[i].x + z.x, s1[i].y + z.y);
+                                const float2 b2 =
+                                    c_make(fmaf(z.x, z.x, s2[i].x), fmaf(z.y, z.y, s2[i].y));
                                 if (rvs && 2 * m + 1 < out_cols) {
                                     reinterpret_cast<float2*>(srow)[m] = a;
                                     reinterpret_cast<float2*>(qrow)[m] = b2;

@@ -34,12 +34,19 @@ class SearchOps:
 
     corr_max(batch (n, h, w), workspace, conv_data, max_map, arg_map, H, W,
              template_index_base, reset, sum_map=None, sumsq_map=None) folds n
-    templates into the maps (and into the sum / sum-of-squares maps if given)."""
+    templates into the maps (and into the float32 sum / sum-of-squares maps if
+    given).  reset: 0 folds into every map, RESET_ALL lets the batch's first
+    template overwrite every map, RESET_SUMS only the sum maps (the maximum
+    keeps running: each batch then yields float32 partial sums)."""
 
     corr_max: Callable
     pack: Callable       # (max_map, arg_map) -> int64 keys
     unpack: Callable     # (keys, max_map, arg_map) -> None (in place)
     workspace: Callable  # (H, W, h, device) -> workspace tensor
+
+
+RESET_ALL = 1   # the batch's first template overwrites every map
+RESET_SUMS = 2  # ... overwrites the sum maps only
 
 
 def search_workspace_elems(H: int, W: int, h: int, chunk: int = 32) -> int:
@@ -65,13 +72,13 @@ def _cuda_corr_max(batch, workspace, conv_data, max_map, arg_map, H, W, template
         st = lib.zfft_padded_real_corr_2d_max_stats(
             batch.data_ptr(), n, h, w, workspace.data_ptr(), workspace.numel() * 8,
             conv_data.data_ptr(), max_map.data_ptr(), arg_map.data_ptr(), sum_map.data_ptr(),
-            sumsq_map.data_ptr(), oy, ox, H, W, int(template_index_base), 1 if reset else 0, dev,
+            sumsq_map.data_ptr(), oy, ox, H, W, int(template_index_base), int(reset), dev,
             stream)
     else:
         st = lib.zfft_padded_real_corr_2d_max(
             batch.data_ptr(), n, h, w, workspace.data_ptr(), workspace.numel() * 8,
             conv_data.data_ptr(), max_map.data_ptr(), arg_map.data_ptr(), oy, ox, H, W,
-            int(template_index_base), 1 if reset else 0, dev, stream)
+            int(template_index_base), 1 if int(reset) == RESET_ALL else 0, dev, stream)
     _lib.check(st)
 
 
@@ -108,7 +115,7 @@ class SearchCheckpoint:
     next_index: int
     max_map: torch.Tensor
     arg_map: torch.Tensor
-    sum_map: Optional[torch.Tensor] = None    # with stats=True
+    sum_map: Optional[torch.Tensor] = None    # with stats=True (float64)
     sumsq_map: Optional[torch.Tensor] = None
 
     def save(self, path: str) -> None:
@@ -148,8 +155,11 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
     next_index with its maps.  The result equals the uninterrupted search's.
 
     stats=True: also the per-pixel sum and sum of squares of the correlations
-    over all templates (float32; summed across ranks with one all-reduce), for
-    z-score normalisation; returns (max_map, arg_map, sum_map, sumsq_map).
+    over all templates, for z-score normalisation; returns (max_map, arg_map,
+    sum_map, sumsq_map).  The kernels sum each batch in float32; the batches
+    (and the ranks, with one all-reduce) are added in float64, so the sums are
+    float64 and their rounding grows with the batch size, not with the
+    number of templates.
 
     shard_base: `templates` is then only this rank's shard (each rank loads
     its own templates), its first template having global index shard_base;
@@ -191,15 +201,18 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
     else:
         max_map = torch.full((oy, ox), float("-inf"), dtype=torch.float32, device=dev)
         arg_map = torch.full((oy, ox), -1, dtype=torch.int32, device=dev)
-    sum_map = sumsq_map = None
+    sum_map = sumsq_map = part_sum = part_sumsq = None
     if stats:
         if resume is not None:
-            sum_map = resume.sum_map.to(device=dev, dtype=torch.float32, copy=True).contiguous()
-            sumsq_map = resume.sumsq_map.to(device=dev, dtype=torch.float32,
+            sum_map = resume.sum_map.to(device=dev, dtype=torch.float64, copy=True).contiguous()
+            sumsq_map = resume.sumsq_map.to(device=dev, dtype=torch.float64,
                                             copy=True).contiguous()
         else:  # an empty shard contributes zeros
-            sum_map = torch.zeros((oy, ox), dtype=torch.float32, device=dev)
-            sumsq_map = torch.zeros((oy, ox), dtype=torch.float32, device=dev)
+            sum_map = torch.zeros((oy, ox), dtype=torch.float64, device=dev)
+            sumsq_map = torch.zeros((oy, ox), dtype=torch.float64, device=dev)
+        # one batch's float32 partial sums (written afresh by every batch)
+        part_sum = torch.empty((oy, ox), dtype=torch.float32, device=dev)
+        part_sumsq = torch.empty((oy, ox), dtype=torch.float32, device=dev)
     nb = min(batch_size, max(hi - lo, 1))
     workspace = ops.workspace(H, W, h, dev)
 
@@ -231,10 +244,13 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
         b1 = min(b0 + nb, hi)
         batch = stage(j % 2, b0, b1)
         if stats:
-            ops.corr_max(batch, workspace, conv_data, max_map, arg_map, H, W, b0, first,
-                         sum_map, sumsq_map)
+            ops.corr_max(batch, workspace, conv_data, max_map, arg_map, H, W, b0,
+                         RESET_ALL if first else RESET_SUMS, part_sum, part_sumsq)
+            sum_map += part_sum
+            sumsq_map += part_sumsq
         else:
-            ops.corr_max(batch, workspace, conv_data, max_map, arg_map, H, W, b0, first)
+            ops.corr_max(batch, workspace, conv_data, max_map, arg_map, H, W, b0,
+                         RESET_ALL if first else 0)
         first = False
         if copy is not None:  # the buffer may be refilled once this batch's kernels ran
             ev = torch.cuda.Event()
