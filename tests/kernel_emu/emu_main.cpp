@@ -297,12 +297,16 @@ void zf::emu_check_prefetch(const void* p, uint32_t bytes) {
     sink = sink + c[0] + c[bytes - 1];
     (void)sink;
 }
-// discard.global.L2 rule: whole 128-byte lines only.
+// discard.global.L2 rule: whole 128-byte lines only.  The line's contents
+// are undefined afterwards: the harness fills it with NaN, so that a line
+// dropped before its last reader shows up in the results.
 void zf::emu_discard_line(const void* p) {
     if (reinterpret_cast<uintptr_t>(p) % 128) {
         std::fprintf(stderr, "misaligned L2 discard %p\n", p);
         std::abort();
     }
+    float* f = static_cast<float*>(const_cast<void*>(p));
+    for (int i = 0; i < 32; ++i) f[i] = NAN;
 }
 // Bulk store rules: 16-byte aligned addresses and sizes, source inside the
 // block's shared memory.
