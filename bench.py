@@ -693,6 +693,16 @@ def run_search_arm(args, world, rank, local):
     clk = clocks.stop()
     ms_total = max_over_ranks(ev0.elapsed_time(ev1), world)
     value = world * SEARCH_PER_STEP * args.steps / (ms_total / 1e3)
+    # One more step, untimed, with events at the search's phase boundaries:
+    # device ms per phase, max over ranks.
+    marks = {}
+    out = template_search(tm, spec, H, W, batch_size=SEARCH_BATCH, full=True, group=group,
+                          stats=args.stats, shard_base=rank * SEARCH_PER_STEP, phase_events=marks)
+    torch.cuda.synchronize()
+    order = [k for k in ("start", "first_copy", "batches", "pack", "reduce", "unpack", "end")
+             if k in marks]
+    phases = {f"{a}->{b}": max_over_ranks(marks[a].elapsed_time(marks[b]), world)
+              for a, b in zip(order, order[1:])}
     if rank == 0:
         peak, peak_src = measured_hbm_peak()
         achieved = SEARCH_ALG_BYTES * value / world / 1e9
@@ -713,6 +723,7 @@ def run_search_arm(args, world, rank, local):
                          "unit_of_work": "one correlation folded into the maps",
                          "peak_source": peak_src},
             "clocks": clk,
+            "phases_ms": phases,
         }
         print(json.dumps(line), flush=True)
     del out

@@ -184,8 +184,13 @@ def test_search_planted_templates_known_answer():
     for (y, x) in pos:
         img[y:y + 384, x:x + 384] += 0.5 * tm[k].numpy()
     spec = torch.from_numpy(O.image_spectrum_T(img)).cuda()
-    mx, am = template_search(tm.pin_memory(), spec, H, H, batch_size=64, full=True)
+    marks = {}
+    mx, am = template_search(tm.pin_memory(), spec, H, H, batch_size=64, full=True,
+                             phase_events=marks)
     torch.cuda.synchronize()
+    assert list(marks) == ["start", "first_copy", "batches"]  # one rank: no reduction phases
+    assert 0 <= marks["start"].elapsed_time(marks["first_copy"]) \
+        <= marks["start"].elapsed_time(marks["batches"])
     mx, am = mx.cpu().numpy(), am.cpu().numpy()
     for (y, x) in pos:
         assert am[y, x] == k

@@ -14,6 +14,7 @@
 #include <cstdlib>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -111,6 +112,20 @@ int tw_offset(int n) {
 // symbol; the device address comes from cudaGetSymbolAddress.
 constexpr size_t kNoAllocBytes = size_t(16) << 20;
 __device__ __align__(256) float2 g_noalloc_ws[kNoAllocBytes / sizeof(float2)];
+
+// The number of visible devices, read once: it cannot change while the
+// process runs, and the calls validate their device index against it.
+cudaError_t device_count(int* n) {
+    static std::atomic<int> cached{-1};
+    int c = cached.load(std::memory_order_relaxed);
+    if (c < 0) {
+        cudaError_t e = cudaGetDeviceCount(&c);
+        if (e != cudaSuccess) return e;
+        cached.store(c, std::memory_order_relaxed);
+    }
+    *n = c;
+    return cudaSuccess;
+}
 
 std::mutex g_init_mu;
 bool g_dev_ready[kMaxDevices];
@@ -344,7 +359,7 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
                     "misaligned pointer: input/output need 4-byte alignment, fft_workspace and "
                     "conv_data 16-byte alignment (TMA copies)");
     int ndev = 0;
-    cudaError_t e = cudaGetDeviceCount(&ndev);
+    cudaError_t e = device_count(&ndev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
     if (device < 0 || device >= ndev || device >= kMaxDevices)
         return fail(ZFFT_ERROR_INVALID_VALUE, "invalid device index %d (%d devices)", device, ndev);
@@ -666,7 +681,7 @@ int zfft_image_spectrum(const float* image, int fft_size_y, int fft_size_x, void
                     "misaligned pointer: image needs 4-byte alignment, conv_data 16-byte "
                     "alignment (TMA copies)");
     int ndev = 0;
-    cudaError_t e = cudaGetDeviceCount(&ndev);
+    cudaError_t e = device_count(&ndev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
     if (device < 0 || device >= ndev || device >= kMaxDevices)
         return fail(ZFFT_ERROR_INVALID_VALUE, "invalid device index %d (%d devices)", device, ndev);
@@ -742,7 +757,7 @@ int launch_keys(bool pack, const float* v_in, float* v_out, const int32_t* i_in,
     g_last_error.clear();
     if (n == 0) return ZFFT_SUCCESS;
     int ndev = 0;
-    cudaError_t e = cudaGetDeviceCount(&ndev);
+    cudaError_t e = device_count(&ndev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
     if (device < 0 || device >= ndev || device >= kMaxDevices)
         return fail(ZFFT_ERROR_INVALID_VALUE, "invalid device index %d (%d devices)", device, ndev);
@@ -795,7 +810,7 @@ int zfft_padded_real_corr_2d_noalloc(const float* input, int batch, int signal_y
                     "zfft_padded_real_corr_2d with a caller-provided workspace",
                     fft_size_y, fft_size_x, need, kNoAllocBytes, kNoAllocBytes / sizeof(float2));
     int ndev = 0;
-    cudaError_t e = cudaGetDeviceCount(&ndev);
+    cudaError_t e = device_count(&ndev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
     if (device < 0 || device >= ndev || device >= kMaxDevices)
         return fail(ZFFT_ERROR_INVALID_VALUE, "invalid device index %d (%d devices)", device, ndev);
@@ -825,7 +840,7 @@ int zfft_check_device_status(int device, void* stream, int* status) {
     if (!status) return fail(ZFFT_ERROR_INVALID_VALUE, "status pointer is null");
     *status = ZFFT_SUCCESS;
     int ndev = 0;
-    cudaError_t e = cudaGetDeviceCount(&ndev);
+    cudaError_t e = device_count(&ndev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
     if (device < 0 || device >= ndev || device >= kMaxDevices)
         return fail(ZFFT_ERROR_INVALID_VALUE, "invalid device index %d (%d devices)", device, ndev);
@@ -851,7 +866,7 @@ int zfft_check_device_status(int device, void* stream, int* status) {
 int zfft_selftest_wait_timeout(int device, void* stream) {
     g_last_error.clear();
     int ndev = 0;
-    cudaError_t e = cudaGetDeviceCount(&ndev);
+    cudaError_t e = device_count(&ndev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
     if (device < 0 || device >= ndev || device >= kMaxDevices)
         return fail(ZFFT_ERROR_INVALID_VALUE, "invalid device index %d (%d devices)", device, ndev);

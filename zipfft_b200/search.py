@@ -138,7 +138,8 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
                     ops: SearchOps = CUDA_OPS, checkpoint_every: int = 0,
                     on_checkpoint: Optional[Callable[[SearchCheckpoint], None]] = None,
                     resume: Optional[SearchCheckpoint] = None, stats: bool = False,
-                    shard_base: Optional[int] = None) -> Tuple[torch.Tensor, ...]:
+                    shard_base: Optional[int] = None,
+                    phase_events: Optional[dict] = None) -> Tuple[torch.Tensor, ...]:
     """Maximum and argmax (global template index) of the correlation per pixel.
 
     templates: (N, h, w) float32 -- the whole set (every rank passes the same
@@ -163,7 +164,13 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
 
     shard_base: `templates` is then only this rank's shard (each rank loads
     its own templates), its first template having global index shard_base;
-    nothing is split further.  The ranks' shards must not overlap."""
+    nothing is split further.  The ranks' shards must not overlap.
+
+    phase_events: a dict that receives timing events recorded on the compute
+    stream at each phase boundary ("start", "first_copy" (the first batch is
+    on the device), "batches", "pack", "reduce", "unpack", "end"; the last
+    four only with more than one rank), for
+    per-phase device times once the stream has been synchronised."""
     import torch.distributed as dist
 
     distributed = dist.is_available() and dist.is_initialized()
@@ -238,11 +245,20 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
             buf.copy_(templates[b0 - off:b1 - off])
         return buf
 
+    def mark(name: str) -> None:
+        if phase_events is not None and compute is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(compute)
+            phase_events[name] = ev
+
+    mark("start")
     # A resumed shard has maps to fold into; a fresh one starts by overwriting.
     first = start == lo
     for j, b0 in enumerate(range(start, hi, nb)):
         b1 = min(b0 + nb, hi)
         batch = stage(j % 2, b0, b1)
+        if j == 0:
+            mark("first_copy")
         if stats:
             ops.corr_max(batch, workspace, conv_data, max_map, arg_map, H, W, b0,
                          RESET_ALL if first else RESET_SUMS, part_sum, part_sumsq)
@@ -262,14 +278,19 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
             on_checkpoint(SearchCheckpoint(N, rank, world, b1, snap(max_map), snap(arg_map),
                                            snap(sum_map), snap(sumsq_map)))
 
+    mark("batches")
     if world > 1:
         keys = ops.pack(max_map, arg_map)
+        mark("pack")
         dist.all_reduce(keys, op=dist.ReduceOp.MAX, group=group)
+        mark("reduce")
         ops.unpack(keys, max_map, arg_map)
+        mark("unpack")
         if stats:
             both = torch.stack([sum_map, sumsq_map])
             dist.all_reduce(both, op=dist.ReduceOp.SUM, group=group)
             sum_map, sumsq_map = both[0], both[1]
+        mark("end")
     if stats:
         return max_map, arg_map, sum_map, sumsq_map
     return max_map, arg_map
