@@ -15,6 +15,8 @@ def test_tc_dft_library_builds_and_exports():
 def test_tc_dft_rejects_bad_arguments_without_a_launch():
     lib = T.load()
     # misaligned pointer and negative column count fail before any CUDA call
-    assert lib.zftc_col_fft4096(ctypes.c_void_p(8), -1, 1, 0, None) == 1
+    assert lib.zftc_col_fft4096(ctypes.c_void_p(8), -1, 1, 1, 0, 0, None) == 1
     assert b"invalid" in lib.zftc_last_error()
-    assert lib.zftc_col_fft4096(ctypes.c_void_p(8), 1, 1, 99, None) == 1
+    assert lib.zftc_col_fft4096(ctypes.c_void_p(16), 4, 0, 1, 0, 0, None) == 1  # passes < 1
+    assert lib.zftc_col_fft4096(ctypes.c_void_p(16), 4, 1, 1, 9, 0, None) == 1  # blocks/SM > 8
+    assert lib.zftc_col_fft4096(ctypes.c_void_p(8), 1, 1, 1, 0, 99, None) == 1

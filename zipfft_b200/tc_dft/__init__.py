@@ -25,7 +25,8 @@ LIB = os.path.join(HERE, "libzftc.so")
 STAMP = LIB + ".stamp"
 _DEPS = [SRC, os.path.join(HERE, "..", "csrc", "fft_core.cuh"),
          os.path.join(HERE, "..", "csrc", "async_copy.cuh")]
-EXPORTS = ("zftc_col_fft4096", "zftc_kernel_info", "zftc_status", "zftc_last_error")
+EXPORTS = ("zftc_col_fft4096", "zftc_kernel_info", "zftc_occupancy", "zftc_status",
+           "zftc_last_error")
 N = 4096
 
 
@@ -71,7 +72,9 @@ def load() -> ctypes.CDLL:
             raise RuntimeError(f"{LIB} is not built: python -c 'import zipfft_b200.tc_dft as t; t.build()'")
         lib = ctypes.CDLL(LIB)
         lib.zftc_col_fft4096.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-                                         ctypes.c_void_p]
+                                         ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+        lib.zftc_occupancy.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                       ctypes.POINTER(ctypes.c_int)]
         lib.zftc_kernel_info.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
                                          ctypes.POINTER(ctypes.c_int)]
         lib.zftc_status.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
@@ -80,9 +83,11 @@ def load() -> ctypes.CDLL:
     return _lib
 
 
-def col_fft4096(x, tensor_cores: bool) -> None:
+def col_fft4096(x, tensor_cores: bool, passes: int = 1, blocks_per_sm: int = 0) -> None:
     """In-place forward FFT of each row of x: (columns, 4096) complex64,
-    contiguous, on a CUDA device; launched on the current stream."""
+    contiguous, on a CUDA device, applied `passes` times; launched on the
+    current stream.  blocks_per_sm > 0 overrides the occupancy calculator's
+    blocks per SM for the persistent grid."""
     import torch
 
     if x.dtype != torch.complex64 or x.dim() != 2 or x.shape[1] != N or not x.is_contiguous() \
@@ -90,7 +95,8 @@ def col_fft4096(x, tensor_cores: bool) -> None:
         raise RuntimeError("expected a contiguous (columns, 4096) complex64 CUDA tensor")
     lib = load()
     dev = x.device.index
-    st = lib.zftc_col_fft4096(x.data_ptr(), x.shape[0], 1 if tensor_cores else 0, dev,
+    st = lib.zftc_col_fft4096(x.data_ptr(), x.shape[0], int(passes), 1 if tensor_cores else 0,
+                              int(blocks_per_sm), dev,
                               torch.cuda.current_stream(dev).cuda_stream)
     if st:
         raise RuntimeError(lib.zftc_last_error().decode())
@@ -103,6 +109,16 @@ def kernel_info(tensor_cores: bool, device: int = 0) -> tuple[int, int]:
     if lib.zftc_kernel_info(1 if tensor_cores else 0, device, ctypes.byref(regs), ctypes.byref(occ)):
         raise RuntimeError(lib.zftc_last_error().decode())
     return regs.value, occ.value
+
+
+def occupancy(tensor_cores: bool, smem: int, device: int = 0) -> int:
+    """Resident blocks per SM of one kernel with `smem` bytes of dynamic
+    shared memory (the occupancy calculator's answer)."""
+    lib = load()
+    occ = ctypes.c_int()
+    if lib.zftc_occupancy(1 if tensor_cores else 0, device, int(smem), ctypes.byref(occ)):
+        raise RuntimeError(lib.zftc_last_error().decode())
+    return occ.value
 
 
 def status(device: int = 0) -> int:

@@ -146,13 +146,16 @@ ZF_DEV void read_row(const unsigned char* buf, int row, float2* v) {
     }
 }
 
-// In-place forward 4096-point FFT of `columns` contiguous columns; one block
-// per column at a time (persistent grid).  tw1[k * 256 + t] = W_4096^(t k),
+// In-place forward 4096-point FFT of `columns` contiguous columns, applied
+// `passes` times to each column between its load and its store (2 passes do
+// twice the arithmetic per byte, like the fused column pass's forward and
+// inverse transforms); one block per column at a time (persistent grid).  tw1[k * 256 + t] = W_4096^(t k),
 // tw2[k * 256 + t] = W_256^((t mod 16) k) (thread t's twiddles, coalesced);
 // bmat: the 32 x 32 real DFT-16 matrix, row n of B = column n of the GEMM
 // (K-major), used by the tensor-core kernel only.
 template <bool TC>
 __global__ void __launch_bounds__(kT) k_col_fft4096(float2* __restrict__ data, int columns,
+                                                    int passes,
                                                     const float2* __restrict__ tw1,
                                                     const float2* __restrict__ tw2,
                                                     const float* __restrict__ bmat,
@@ -236,48 +239,52 @@ __global__ void __launch_bounds__(kT) k_col_fft4096(float2* __restrict__ data, i
         float2 v[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] = x[t + kT * j];
-        // Stage 1: row m = t holds x[m + 256 n2] at position n2.
-        if constexpr (TC) {
-            write_row_split(a_hi, a_lo, t, v);
-            mma_round(v);
-        } else {
-            zf::dft16<false>(v);
+#pragma unroll 1
+        for (int pass = 0; pass < passes; ++pass) {
+            // Stage 1: row m = t holds x[m + 256 n2] at position n2.
+            if constexpr (TC) {
+                write_row_split(a_hi, a_lo, t, v);
+                mma_round(v);
+            } else {
+                zf::dft16<false>(v);
+            }
+#pragma unroll
+            for (int k = 1; k < 16; ++k) v[k] = zf::c_mul(v[k], tw1[k * kT + t]);
+            // Stage 2: value k0 of row m = n0 + 16 n1 goes to row 16 k0 + n0,
+            // position n1.
+            const int n0 = t & 15, n1 = t >> 4;
+            if constexpr (TC) {
+#pragma unroll
+                for (int k = 0; k < 16; ++k) write_pos_split(a_hi, a_lo, k * 16 + n0, n1, v[k]);
+                mma_round(v);
+            } else {
+                __syncthreads();  // earlier reads of the buffer are done
+#pragma unroll
+                for (int k = 0; k < 16; ++k) write_pos(a_hi, k * 16 + n0, n1, v[k]);
+                __syncthreads();
+                read_row(a_hi, t, v);
+                zf::dft16<false>(v);
+            }
+            // Row t = 16 k0 + n0 holds value k1: twiddle W_256^(n0 k1).
+#pragma unroll
+            for (int k = 1; k < 16; ++k) v[k] = zf::c_mul(v[k], tw2[k * kT + t]);
+            // Stage 3: value k1 of row 16 k0 + n0 goes to row 16 k1 + k0,
+            // position n0.
+            if constexpr (TC) {
+#pragma unroll
+                for (int k = 0; k < 16; ++k) write_pos_split(a_hi, a_lo, k * 16 + n1, n0, v[k]);
+                mma_round(v);
+            } else {
+                __syncthreads();
+#pragma unroll
+                for (int k = 0; k < 16; ++k) write_pos(a_hi, k * 16 + n1, n0, v[k]);
+                __syncthreads();
+                read_row(a_hi, t, v);
+                zf::dft16<false>(v);
+            }
+            // Row t = 16 k1 + k0 holds X[k0 + 16 k1 + 256 k2] = X[t + 256 k2] at k2:
+            // the layout of the input, so another pass can follow directly.
         }
-#pragma unroll
-        for (int k = 1; k < 16; ++k) v[k] = zf::c_mul(v[k], tw1[k * kT + t]);
-        // Stage 2: value k0 of row m = n0 + 16 n1 goes to row 16 k0 + n0,
-        // position n1.
-        const int n0 = t & 15, n1 = t >> 4;
-        if constexpr (TC) {
-#pragma unroll
-            for (int k = 0; k < 16; ++k) write_pos_split(a_hi, a_lo, k * 16 + n0, n1, v[k]);
-            mma_round(v);
-        } else {
-            __syncthreads();  // earlier reads of the buffer are done
-#pragma unroll
-            for (int k = 0; k < 16; ++k) write_pos(a_hi, k * 16 + n0, n1, v[k]);
-            __syncthreads();
-            read_row(a_hi, t, v);
-            zf::dft16<false>(v);
-        }
-        // Row t = 16 k0 + n0 holds value k1: twiddle W_256^(n0 k1).
-#pragma unroll
-        for (int k = 1; k < 16; ++k) v[k] = zf::c_mul(v[k], tw2[k * kT + t]);
-        // Stage 3: value k1 of row 16 k0 + n0 goes to row 16 k1 + k0,
-        // position n0.
-        if constexpr (TC) {
-#pragma unroll
-            for (int k = 0; k < 16; ++k) write_pos_split(a_hi, a_lo, k * 16 + n1, n0, v[k]);
-            mma_round(v);
-        } else {
-            __syncthreads();
-#pragma unroll
-            for (int k = 0; k < 16; ++k) write_pos(a_hi, k * 16 + n1, n0, v[k]);
-            __syncthreads();
-            read_row(a_hi, t, v);
-            zf::dft16<false>(v);
-        }
-        // Row t = 16 k1 + k0 holds X[k0 + 16 k1 + 256 k2] = X[t + 256 k2] at k2.
 #pragma unroll
         for (int j = 0; j < 16; ++j) x[t + kT * j] = v[j];
         if constexpr (TC) {
@@ -417,14 +424,17 @@ int ensure(int dev) {
 ZFTC_API const char* zftc_last_error() { return g_err; }
 
 // In-place forward 4096-point FFTs of `columns` contiguous columns of complex64
-// (column c at data + 4096 c); tensor_cores selects the tcgen05 kernel.
+// (column c at data + 4096 c), `passes` times each; tensor_cores selects the
+// tcgen05 kernel; blocks_per_sm = 0 sizes the persistent grid by occupancy.
 // Returns 0, or 1 with zftc_last_error() set.
-ZFTC_API int zftc_col_fft4096(void* data, int columns, int tensor_cores, int device, void* stream) {
+ZFTC_API int zftc_col_fft4096(void* data, int columns, int passes, int tensor_cores, int blocks_per_sm,
+                              int device, void* stream) {
     if (device < 0 || device >= kMaxDev) {
         snprintf(g_err, sizeof g_err, "invalid device %d", device);
         return 1;
     }
-    if (columns < 0 || (columns > 0 && !data) || (reinterpret_cast<uintptr_t>(data) & 15u)) {
+    if (columns < 0 || passes < 1 || blocks_per_sm < 0 || blocks_per_sm > 8 || (columns > 0 && !data) ||
+        (reinterpret_cast<uintptr_t>(data) & 15u)) {
         snprintf(g_err, sizeof g_err, "invalid arguments");
         return 1;
     }
@@ -434,7 +444,10 @@ ZFTC_API int zftc_col_fft4096(void* data, int columns, int tensor_cores, int dev
     if (columns == 0) return 0;
     const DevState& st = g_dev[device];
     const int tc = tensor_cores ? 1 : 0;
-    int grid = st.sms * st.occ[tc];
+    // blocks_per_sm > 0: launch that many blocks per SM instead of the
+    // occupancy calculator's figure (the hardware runs the surplus as later
+    // waves if they do not fit).
+    int grid = st.sms * (blocks_per_sm > 0 ? blocks_per_sm : st.occ[tc]);
     if (grid > columns) grid = columns;
     if (grid < 1) {
         snprintf(g_err, sizeof g_err, "kernel does not fit on an SM");
@@ -443,10 +456,10 @@ ZFTC_API int zftc_col_fft4096(void* data, int columns, int tensor_cores, int dev
     auto s = static_cast<cudaStream_t>(stream);
     if (tc)
         zftc::k_col_fft4096<true><<<grid, zftc::kT, zftc::kSmemTc, s>>>(
-            static_cast<float2*>(data), columns, st.tw1, st.tw2, st.bmat, st.status);
+            static_cast<float2*>(data), columns, passes, st.tw1, st.tw2, st.bmat, st.status);
     else
         zftc::k_col_fft4096<false><<<grid, zftc::kT, zftc::kSmemCuda, s>>>(
-            static_cast<float2*>(data), columns, st.tw1, st.tw2, st.bmat, st.status);
+            static_cast<float2*>(data), columns, passes, st.tw1, st.tw2, st.bmat, st.status);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : fail_cuda("launch", e);
 }
@@ -461,6 +474,21 @@ ZFTC_API int zftc_kernel_info(int tensor_cores, int device, int* regs, int* bloc
     *regs = g_dev[device].regs[tc];
     *blocks_per_sm = g_dev[device].occ[tc];
     return 0;
+}
+
+// Resident blocks per SM of one kernel with `smem` bytes of dynamic shared
+// memory, as the occupancy calculator reports it.
+ZFTC_API int zftc_occupancy(int tensor_cores, int device, int smem, int* blocks_per_sm) {
+    if (device < 0 || device >= kMaxDev) return 1;
+    DeviceSwitch sw(device);
+    if (sw.err != cudaSuccess) return fail_cuda("cudaSetDevice", sw.err);
+    if (ensure(device)) return 1;
+    const cudaError_t e =
+        tensor_cores ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, zftc::k_col_fft4096<true>,
+                                                                     zftc::kT, size_t(smem))
+                     : cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, zftc::k_col_fft4096<false>,
+                                                                     zftc::kT, size_t(smem));
+    return e == cudaSuccess ? 0 : fail_cuda("occupancy", e);
 }
 
 // The device status word (4: a bounded wait gave up), then cleared.
