@@ -30,6 +30,18 @@ __all__ = ["corr", "conv", "corr_max", "image_spectrum", "get_supported_conv_con
            "supported_fft_sizes", "workspace_bytes"]
 
 
+# The current stream's handle without building a torch.cuda.Stream object
+# (the public call below is the fallback).
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _current_stream(device: int) -> int:
+    """Handle of torch's current CUDA stream on `device`."""
+    if _raw_stream is not None:
+        return _raw_stream(device)
+    return torch.cuda.current_stream(device).cuda_stream
+
+
 def _check(cond: bool, msg: str) -> None:
     if not cond:
         raise RuntimeError(msg)
@@ -45,16 +57,16 @@ def _validate(input: torch.Tensor, fft_workspace: torch.Tensor, conv_data: torch
     instead); its contiguity is not checked.  Every caller whose `output`
     receives the maps leaves this False, so an expanded or overlapping output
     (stride 0 over the batch) is rejected before anything launches."""
-    _check(input.device.type == "cuda", "Input tensor must be on CUDA device")
-    _check(fft_workspace.device.type == "cuda", "FFT workspace tensor must be on CUDA device")
-    _check(conv_data.device.type == "cuda", "Convolution data tensor must be on CUDA device")
-    _check(output.device.type == "cuda", "Output tensor must be on CUDA device")
-    ref = input.device
-    _check(fft_workspace.device == ref,
-           "FFT workspace tensor must be on the same device as the input tensor")
-    _check(conv_data.device == ref,
-           "Convolution data tensor must be on the same device as the input tensor")
-    _check(output.device == ref, "Output tensor must be on the same device as the input tensor")
+    # Each tensor's attributes are read once (a torch attribute read costs
+    # a few hundred ns of host time; the small-image calls take ~25 us).
+    idev, wdev, cdev, odev = input.device, fft_workspace.device, conv_data.device, output.device
+    _check(idev.type == "cuda", "Input tensor must be on CUDA device")
+    _check(wdev.type == "cuda", "FFT workspace tensor must be on CUDA device")
+    _check(cdev.type == "cuda", "Convolution data tensor must be on CUDA device")
+    _check(odev.type == "cuda", "Output tensor must be on CUDA device")
+    _check(wdev == idev, "FFT workspace tensor must be on the same device as the input tensor")
+    _check(cdev == idev, "Convolution data tensor must be on the same device as the input tensor")
+    _check(odev == idev, "Output tensor must be on the same device as the input tensor")
     _check(input.dtype == torch.float32, "Input tensor must be of type torch.float32")
     _check(fft_workspace.dtype == torch.complex64,
            "FFT workspace tensor must be of type torch.complex64 (float2)")
@@ -62,49 +74,48 @@ def _validate(input: torch.Tensor, fft_workspace: torch.Tensor, conv_data: torch
            "Convolution data tensor must be of type torch.complex64 (float2)")
     _check(output.dtype == torch.float32, "Output tensor must be of type torch.float32")
 
-    if input.dim() == 2:
-        batch, sy, sx = 1, input.size(0), input.size(1)
-    elif input.dim() == 3:
-        batch, sy, sx = input.size(0), input.size(1), input.size(2)
+    ishape, wshape, cshape, oshape = input.shape, fft_workspace.shape, conv_data.shape, output.shape
+    ndim = len(ishape)
+    if ndim == 2:
+        batch, sy, sx = 1, ishape[0], ishape[1]
+    elif ndim == 3:
+        batch, sy, sx = ishape
     else:
-        raise RuntimeError(f"Input tensor must be 2D or 3D. Got {input.dim()}D.")
+        raise RuntimeError(f"Input tensor must be 2D or 3D. Got {ndim}D.")
 
     stride = fft_size_x // 2 + 1
-    _check(fft_workspace.dim() == input.dim(),
+    _check(len(wshape) == ndim,
            "FFT workspace tensor must have the same number of dimensions as the input tensor")
-    _check(fft_workspace.size(-1) == stride,
-           "FFT workspace tensor last dimension must be fft_size_x/2 + 1")
-    _check(fft_workspace.size(-2) == fft_size_y,
+    _check(wshape[-1] == stride, "FFT workspace tensor last dimension must be fft_size_x/2 + 1")
+    _check(wshape[-2] == fft_size_y,
            "FFT workspace tensor second-to-last dimension must be fft_size_y")
     if batch > 1:
-        _check(fft_workspace.size(0) == batch,
+        _check(wshape[0] == batch,
                "FFT workspace tensor first dimension (batch) must match input batch size")
 
     # The two messages below are the reference's text verbatim (binding.cu:252-255).
-    _check(conv_data.dim() == 2, f"Convolution data tensor must be 2D. Got {conv_data.dim()}D.")
-    _check(conv_data.size(0) == stride,
-           "Convolution data tensor first dimension must match fft_size_y")
-    _check(conv_data.size(1) == fft_size_y,
+    _check(len(cshape) == 2, f"Convolution data tensor must be 2D. Got {len(cshape)}D.")
+    _check(cshape[0] == stride, "Convolution data tensor first dimension must match fft_size_y")
+    _check(cshape[1] == fft_size_y,
            "Convolution data tensor second dimension must be fft_size_x/2 + 1")
 
     vx, vy = fft_size_x - sx + 1, fft_size_y - sy + 1
-    _check(output.dim() == input.dim(),
+    _check(len(oshape) == ndim,
            "Output tensor must have the same number of dimensions as the input tensor")
-    full = output.size(-1) == fft_size_x and output.size(-2) == fft_size_y
+    oy, ox = oshape[-2], oshape[-1]
+    full = ox == fft_size_x and oy == fft_size_y
     if not full:
-        _check(output.size(-1) == vx,
-               "Output tensor last dimension must be fft_size_x - signal_length_x + 1")
-        _check(output.size(-2) == vy,
+        _check(ox == vx, "Output tensor last dimension must be fft_size_x - signal_length_x + 1")
+        _check(oy == vy,
                "Output tensor second-to-last dimension must be fft_size_y - signal_length_y + 1")
-    if output.dim() == 3:
-        _check(output.size(0) == batch, "Output tensor first dimension (batch) must match input "
-                                        "batch size")
-    for name, t in (("Input", input), ("FFT workspace", fft_workspace),
-                    ("Convolution data", conv_data), ("Output", output)):
-        if t is output and output_is_shape_stand_in:
-            continue
-        _check(t.is_contiguous(), f"{name} tensor must be contiguous")
-    return batch, sy, sx, output.size(-2), output.size(-1)
+    if len(oshape) == 3:
+        _check(oshape[0] == batch, "Output tensor first dimension (batch) must match input "
+                                   "batch size")
+    _check(input.is_contiguous(), "Input tensor must be contiguous")
+    _check(fft_workspace.is_contiguous(), "FFT workspace tensor must be contiguous")
+    _check(conv_data.is_contiguous(), "Convolution data tensor must be contiguous")
+    _check(output_is_shape_stand_in or output.is_contiguous(), "Output tensor must be contiguous")
+    return batch, sy, sx, oy, ox
 
 
 def _run(fn_name: str, input, fft_workspace, conv_data, output, fft_size_y: int,
@@ -113,7 +124,7 @@ def _run(fn_name: str, input, fft_workspace, conv_data, output, fft_size_y: int,
                                       int(fft_size_x))
     lib = _lib.load()
     device = input.device.index if input.device.index is not None else torch.cuda.current_device()
-    stream = torch.cuda.current_stream(device).cuda_stream
+    stream = _current_stream(device)
     ws_bytes = fft_workspace.numel() * fft_workspace.element_size()
     status = getattr(lib, fn_name)(input.data_ptr(), batch, sy, sx, fft_workspace.data_ptr(),
                                    ws_bytes, conv_data.data_ptr(), output.data_ptr(), oy, ox,
@@ -145,7 +156,7 @@ def corr(input: torch.Tensor, fft_workspace: torch.Tensor, conv_data: torch.Tens
            f"Peaks tensor must be contiguous with {batch} elements (one per template)")
     lib = _lib.load()
     device = input.device.index if input.device.index is not None else torch.cuda.current_device()
-    stream = torch.cuda.current_stream(device).cuda_stream
+    stream = _current_stream(device)
     ws_bytes = fft_workspace.numel() * fft_workspace.element_size()
     status = lib.zfft_padded_real_corr_2d_peaks(input.data_ptr(), batch, sy, sx,
                                                 fft_workspace.data_ptr(), ws_bytes,
@@ -203,7 +214,7 @@ def corr_max(input: torch.Tensor, fft_workspace: torch.Tensor, conv_data: torch.
                                       int(fft_size_x), output_is_shape_stand_in=True)
     lib = _lib.load()
     device = input.device.index if input.device.index is not None else torch.cuda.current_device()
-    stream = torch.cuda.current_stream(device).cuda_stream
+    stream = _current_stream(device)
     ws_bytes = fft_workspace.numel() * fft_workspace.element_size()
     if stats:
         status = lib.zfft_padded_real_corr_2d_max_stats(
@@ -247,7 +258,7 @@ def image_spectrum(image: torch.Tensor, conv_data: torch.Tensor = None) -> torch
     _check(conv_data.is_contiguous(), "Convolution data tensor must be contiguous")
     lib = _lib.load()
     device = image.device.index if image.device.index is not None else torch.cuda.current_device()
-    stream = torch.cuda.current_stream(device).cuda_stream
+    stream = _current_stream(device)
     status = lib.zfft_image_spectrum(image.data_ptr(), H, W, conv_data.data_ptr(),
                                      conv_data.numel() * conv_data.element_size(), device, stream)
     _lib.check(status)
