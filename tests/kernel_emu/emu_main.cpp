@@ -494,7 +494,10 @@ void run_c2r(const float2* Q, int H, float* out, int* arg, float* sum, float* su
     using C = zf::C2rCfg<W2>;
     zf::CUtensorMap map{reinterpret_cast<const unsigned char*>(Q), H, W2 * nt, (long long)H * 8,
                         C::RPB, C::BOXK, 8};
-    int groups = (orows + C::RPB - 1) / C::RPB * nt;
+    // As the library's launcher: the running-map modes give each block whole
+    // row groups (all nt templates of each), the map modes (template, group)
+    // units.
+    int groups = (orows + C::RPB - 1) / C::RPB * (arg ? 1 : nt);
     const auto ttr = thread_twiddles<RowPlanOf<2 * W2>, 2 * W2>(tw);
     const auto ttc = thread_twiddles<ColPlanOf<2 * W2>, 2 * W2>(tw);
     int grid = groups < cap ? groups : cap;
@@ -629,12 +632,13 @@ int main(int argc, char** argv) {
     const bool max_mode = hd[12] == 1 || hd[12] == 2;  // fold into running max / argmax maps
     const bool stats = hd[12] == 2;                    // ... and into sum / sum-of-squares maps
     const bool peaks_mode = hd[12] == 3;               // maps plus per-template peaks
-    const int group = max_mode ? 0 : (hd[13] & 0xFFFF);  // >= 2: batched groups
+    const int group = hd[13] & 0xFFFF;                   // >= 2: batched groups
     const bool poison = (hd[13] >> 16) & 1;              // workspace starts as NaN
     emu_defer_loads = (hd[13] >> 17) & 1;                // TMA loads land at the wait
     // max_mode 2 with bit 18: every second template starts a new "batch"
     // whose first template overwrites only the sum maps (reset kResetSums),
     // as the search's per-batch partial sums do; the maximum keeps running.
+    // With batched groups, every group after the first starts a new batch.
     const bool sum_batches = (hd[13] >> 18) & 1;
     const int W2 = W / 2;
     std::vector<float> tm((size_t)B * sy * sx);
@@ -672,9 +676,13 @@ int main(int argc, char** argv) {
         col(H, conj, nz_col, Q, Q, H, spec.data(), twH.data(), sy, W2, oy, cap, n, q_elems,
             q_elems);
         // the tile map spans the whole group's slices, as on the device
-        c2r(W, Q, H, out.data() + (size_t)t0 * oy * ox, nullptr, nullptr, nullptr,
-            peaks_mode ? peak_keys.data() + t0 : nullptr, twW.data(), oy, ox, 0, 0, cap, n,
-            (long long)oy * ox);
+        if (max_mode)  // the group's templates folded into the running maps
+            c2r(W, Q, H, out.data(), arg.data(), sum_p, sumsq_p, nullptr, twW.data(), oy, ox, t0,
+                t0 == 0 ? zf::kResetMax : (sum_batches ? zf::kResetSums : 0), cap, n, 0);
+        else
+            c2r(W, Q, H, out.data() + (size_t)t0 * oy * ox, nullptr, nullptr, nullptr,
+                peaks_mode ? peak_keys.data() + t0 : nullptr, twW.data(), oy, ox, 0, 0, cap, n,
+                (long long)oy * ox);
     }
     const int step = chunk > 0 ? chunk : 1;
     for (int t0 = 0; group < 2 && t0 < B; t0 += step) {

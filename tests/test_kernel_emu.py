@@ -252,6 +252,8 @@ def test_emulated_pair_kernel_ignores_stale_rows(emu, tmp_path):
     (3, 12, 9, 128, 128, True, True, 0, 1, 0),      # running max / argmax
     (3, 12, 9, 128, 128, True, False, 0, 2, 0),     # ... with sum / sum of squares
     (3, 12, 10, 64, 256, True, False, 0, 3, 0),     # per-template peaks
+    (5, 12, 9, 64, 128, True, True, 0, 1, 2),       # grouped running max / argmax
+    (5, 12, 10, 64, 256, True, False, 0, 2, 3),     # ... with sums, valid crop
 ], ids=lambda c: str(c))
 def test_emulated_kernels_with_late_tma_arrival(emu, tmp_path, case):
     """Every TMA load lands only when a thread polls its barrier, the latest
@@ -279,15 +281,43 @@ def test_emulated_kernels_with_late_tma_arrival(emu, tmp_path, case):
         assert np.array_equal(got[1], out.reshape(B, -1).max(axis=1))
 
 
-def test_emulated_stats_batches_restart_sums_keep_max(emu, tmp_path):
+@pytest.mark.parametrize("group", [0, 2])
+def test_emulated_stats_batches_restart_sums_keep_max(emu, tmp_path, group):
     """reset = kResetSums on a batch's first template (the search's per-batch
     partial sums): the sum maps restart there, the maximum and argmax keep
-    folding every template."""
+    folding every template.  group = 2: batched groups of two templates per
+    launch, each group after the first a new batch."""
     B = 5
     (mx, am, sm, sq), ref = run_emu(emu, tmp_path, B, 12, 9, 64, 128, True, True,
-                                    max_mode=2, sum_batches=True)
+                                    max_mode=2, sum_batches=True, group=group)
     tol = 1e-5 * np.abs(ref).max()
     assert np.allclose(mx, ref.max(axis=0), rtol=0, atol=tol)
     last = ref[4:]  # templates 0-1, 2-3 and 4 form the batches
     assert np.allclose(sm, last.sum(axis=0), rtol=0, atol=tol)
     assert np.allclose(sq, (last ** 2).sum(axis=0), rtol=0, atol=tol * np.abs(ref).max())
+
+
+@pytest.mark.parametrize("group,W,full,sx,max_mode", [
+    (2, 128, True, 9, 1), (3, 128, False, 10, 1), (5, 2048, True, 9, 1),
+    (2, 256, True, 9, 2), (4, 240, False, 9, 2)])
+def test_emulated_grouped_running_maps(emu, tmp_path, group, W, full, sx, max_mode):
+    """Running maps with several templates per launch (batched groups): each
+    block folds a row group's templates one after another into the maps, with
+    3 blocks for more row groups than that (every block takes several groups).
+    Same maxima, argmax (ties excluded) and sums as one template per launch."""
+    B, H = 5, 64
+    got, ref = run_emu(emu, tmp_path, B, 12, sx, H, W, True, full, max_mode=max_mode,
+                       group=group)
+    peak = np.abs(ref).max()
+    assert np.allclose(got[0], ref.max(axis=0), rtol=0, atol=1e-5 * peak)
+    order = np.sort(ref, axis=0)
+    sure = order[-1] - order[-2] > 1e-4 * peak
+    assert sure.mean() > 0.99
+    assert np.array_equal(got[1][sure], ref.argmax(axis=0)[sure])
+    if max_mode == 2:
+        assert O.rel_l2(ref.sum(axis=0), got[2]) < 1e-5
+        assert O.rel_l2((ref ** 2).sum(axis=0), got[3]) < 1e-5
+    one, _ = run_emu(emu, tmp_path, B, 12, sx, H, W, True, full, max_mode=max_mode)
+    # the same per-pixel arithmetic in the same template order: bit-identical
+    for a, b in zip(got, one):
+        assert np.array_equal(a, b)

@@ -400,18 +400,25 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
     }
     float2* Rregion = Q + q_elems;
 
-    // Batched groups: when at least two whole Q slices fit in the workspace
-    // and together within kBatchL2Bytes, the templates of a group go through
-    // each kernel in one launch, each in its own slice (its row spectra first
-    // in rows [0, h) of the slice).  Maps only: the running maps need the
-    // templates one after another.
+    // Batched groups: when at least two whole Q slices fit in the workspace,
+    // the templates of a group go through each kernel in one launch, each in
+    // its own slice (its row spectra first in rows [0, h) of the slice).
+    // Maps: only while the group's slices fit within kBatchL2Bytes (small
+    // images, which then never leave L2).  Running maps: up to kMaxChunk
+    // slices in HBM; the inverse row pass folds a row group's templates one
+    // after another into map rows that stay in L2, instead of streaming the
+    // whole maps through DRAM for every template, and the column pass reads
+    // each spectrum column from DRAM once per group.
     long long group = 0;
-    if (!arg && batch > 1) {
+    if (batch > 1) {
         const long long fit_ws = (long long)(ws_bytes / sizeof(float2)) / q_elems;
-        const long long fit_l2 = kBatchL2Bytes / (q_elems * (long long)sizeof(float2));
-        group = batch;
-        if (fit_ws < group) group = fit_ws;
-        if (fit_l2 < group) group = fit_l2;
+        group = batch < fit_ws ? batch : fit_ws;
+        if (!arg) {
+            const long long fit_l2 = kBatchL2Bytes / (q_elems * (long long)sizeof(float2));
+            if (fit_l2 < group) group = fit_l2;
+        } else if (group > kMaxChunk) {
+            group = kMaxChunk;
+        }
     }
 
     CUtensorMap qmap;
@@ -444,9 +451,13 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
             timer_close(1, m, s);
             if ((e = trace_sync(s, "k_col_fused group", t0)) != cudaSuccess) return cuda_fail(e, "k_col_fused");
             m = timer_mark(s);
-            e = c2r(&qmap, output + (size_t)t0 * oy * ox, nullptr, nullptr, nullptr,
-                    peak_keys ? peak_keys + t0 : nullptr, twW, oy, ox, ox, 0, 0, n,
-                    (long long)oy * ox, status, device, s);
+            if (arg)
+                e = c2r(&qmap, output, arg, sum, sumsq, nullptr, twW, oy, ox, ox, tindex_base + t0,
+                        t0 == 0 ? reset : 0, n, 0, status, device, s);
+            else
+                e = c2r(&qmap, output + (size_t)t0 * oy * ox, nullptr, nullptr, nullptr,
+                        peak_keys ? peak_keys + t0 : nullptr, twW, oy, ox, ox, 0, 0, n,
+                        (long long)oy * ox, status, device, s);
             if (e != cudaSuccess) return cuda_fail(e, "row c2r launch");
             timer_close(2, m, s);
             if ((e = trace_sync(s, "k_row_c2r group", t0)) != cudaSuccess) return cuda_fail(e, "k_row_c2r");

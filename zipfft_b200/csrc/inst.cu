@@ -158,7 +158,11 @@ cudaError_t c2r_t(const CUtensorMap* qmap, float* out, int* arg, float* sum, flo
     int cap = 0;
     cudaError_t e = configure(kernel, st, C::SMEM, C::THREADS, device, &cap);
     if (e != cudaSuccess) return e;
-    const long long units = (long long)((out_rows + C::RPB - 1) / C::RPB) * ntemplates;
+    // The running-map modes hand each block whole row groups (all of the
+    // launch's templates for each), the map modes (template, group) units.
+    const long long groups = (out_rows + C::RPB - 1) / C::RPB;
+    const long long units = (MODE == kRunningMax || MODE == kRunningStats) ? groups
+                                                                           : groups * ntemplates;
     const int grid = (int)(units < cap ? units : cap);
     return launch_pdl(kernel, dim3(grid), C::THREADS, C::SMEM, s, *qmap, out, arg, sum, sumsq, peak,
                       tw, g_tt[device].row, out_rows, out_cols, out_pitch, tindex, reset,
@@ -257,14 +261,17 @@ cudaError_t ZF_CAT(launch_row_c2r_, ZF_SIZE)(const CUtensorMap* qmap, float* out
                                              long long out_tstride, int* status, int device,
                                              cudaStream_t s) {
     constexpr int W2 = ZF_SIZE / 2;
-    if (arg != nullptr && ntemplates != 1) return cudaErrorInvalidValue;
+    if (ntemplates < 1) return cudaErrorInvalidValue;
+    // Running maps: ntemplates consecutive templates (indices tindex, ...)
+    // folded into the same maps (out_tstride unused).
     if (arg != nullptr && sum != nullptr)
         return c2r_t<W2, kRunningStats>(qmap, out, arg, sum, sumsq, nullptr, tw, out_rows,
-                                        out_cols, out_pitch, tindex, reset, 1, 0, status, device,
-                                        s);
+                                        out_cols, out_pitch, tindex, reset, ntemplates, 0, status,
+                                        device, s);
     if (arg != nullptr)
         return c2r_t<W2, kRunningMax>(qmap, out, arg, nullptr, nullptr, nullptr, tw, out_rows,
-                                      out_cols, out_pitch, tindex, reset, 1, 0, status, device, s);
+                                      out_cols, out_pitch, tindex, reset, ntemplates, 0, status,
+                                      device, s);
     // Maps.  Full-width rows that are all 8-byte aligned: the W/2-point form,
     // whose epilogue writes each output pair with one 8-byte store.  Cropped
     // or misaligned rows (the reference's valid crop, e.g. 3841 wide): the

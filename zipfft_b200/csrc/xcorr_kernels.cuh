@@ -255,8 +255,16 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
     const uint32_t r_bytes = (uint32_t)round_up(h, 2) * 8u;
     // Units (template, column group): ntemplates templates of W2 + 1 virtual
     // columns each, template j's Q and R at Q + j q_tstride, R + j r_tstride.
+    // Column-major order: the templates of a column group are consecutive
+    // units, so neighbouring blocks read the same spectrum columns at about
+    // the same time and all but the first find them in L2.
     const int cgroups = (W2 + C::FPB) / C::FPB;
     const int units = cgroups * ntemplates;
+    auto unit_cols = [&](int u, int& tj, int& vc0) {
+        const int cg = u / ntemplates;
+        tj = u - cg * ntemplates;
+        vc0 = cg * C::FPB;
+    };
     // L2 policy: template columns stream through (read once); the spectrum,
     // read once per template but by every template, keeps the normal policy
     // (some of it then survives in L2 for the next template: measured faster
@@ -271,7 +279,8 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
     // part (written by the row kernel before this one) separately, both
     // completing on the buffer's barrier.
     auto issue_spec = [&](int b, int u) {
-        const int tj = u / cgroups, vc0 = (u - tj * cgroups) * C::FPB;
+        int tj, vc0;
+        unit_cols(u, tj, vc0);
         uint32_t bytes = 0;
         for (int j = 0; j < C::FPB; ++j)
             if (vc0 + j <= W2) bytes += H * 8u + r_bytes;
@@ -284,7 +293,8 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
         }
     };
     auto issue_r = [&](int b, int u) {
-        const int tj = u / cgroups, vc0 = (u - tj * cgroups) * C::FPB;
+        int tj, vc0;
+        unit_cols(u, tj, vc0);
         const float2* Rj = R + tj * r_tstride;
         for (int j = 0; j < C::FPB; ++j) {
             const int vc = vc0 + j;
@@ -316,7 +326,8 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
     for (int it = 0; u < units; ++it, u += gridDim.x) {
         const int b = it & 1;
         const uint32_t parity = (it >> 1) & 1;
-        const int tj = u / cgroups, vc0 = (u - tj * cgroups) * C::FPB;
+        int tj, vc0;
+        unit_cols(u, tj, vc0);
         float2* Qj = Q + tj * q_tstride;
         const float2* Rj = R + tj * r_tstride;
         const bool more = u + (int)gridDim.x < units;
@@ -684,6 +695,14 @@ ZF_DEV void fold_warp_peak(float v, unsigned* key) {
 // pitch; reset & (kResetMax | kResetSums) overwrites them instead, so that a
 // caller can start float32 partial sums per batch and accumulate the batches
 // at higher precision while the maximum keeps running).
+//
+// Several templates per launch: in the map modes the units (template, row
+// group) are strided over the grid.  In the running-map modes each block owns
+// whole row groups and folds the launch's templates into a group one after
+// another, template j with index tindex + j (reset applies to j = 0 only):
+// every pixel's updates then come from one block in template order (ties keep
+// the lowest index), and the group's map rows stay hot in L2 across the
+// templates instead of making a DRAM round trip per template.
 template <int W2, int MODE>
 __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     k_row_c2r(const __grid_constant__ CUtensorMap qmap, float* __restrict__ out,
@@ -728,17 +747,29 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     pdl_wait_prerequisites();
 
     // Units (template, row group): template j's Q is columns [j W2, (j+1) W2)
-    // of the tile map, its map out + j out_tstride and its peak peak[j]
-    // (the running-map modes take one template per launch).
+    // of the tile map, its map out + j out_tstride and its peak peak[j].
+    // This block's k-th unit: see the kernel's comment for the two orders.
+    constexpr bool kRunning = MODE == kRunningMax || MODE == kRunningStats;
     const int ngroups = (out_rows + C::RPB - 1) / C::RPB;
     const int units = ngroups * ntemplates;
+    auto unit_of = [&](int k, int& tj, int& grp) -> bool {
+        if constexpr (kRunning) {
+            tj = k % ntemplates;
+            grp = (int)blockIdx.x + (k / ntemplates) * (int)gridDim.x;
+            return grp < ngroups;
+        } else {
+            const int uu = (int)blockIdx.x + k * (int)gridDim.x;
+            tj = uu / ngroups;
+            grp = uu - tj * ngroups;
+            return uu < units;
+        }
+    };
 
     // L2 policy: Q lines stay resident (the next template's column pass
     // overwrites them there without a DRAM round trip); output rows stream out.
     const uint64_t pol_keep = l2_evict_last();
     const uint64_t pol_stream = l2_evict_first();
-    auto issue = [&](int b, int u) {
-        const int tj = u / ngroups, grp = u - tj * ngroups;
+    auto issue = [&](int b, int tj, int grp) {
         mbar_arrive_expect_tx(&mbar[b], (uint32_t)(W2 * C::RPB * 8));
         for (int k0 = 0; k0 < W2; k0 += C::BOXK)
             tma_load_2d(qbase + b * C::QB + k0 * C::RPB, &qmap, grp * C::RPB, tj * W2 + k0,
@@ -748,10 +779,10 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     // Output rows leave through per-thread stores: staging them for bulk
     // stores needs one more block barrier per group, which cost more than the
     // store-queue stalls it removed.
-    // Running-map modes: L2 prefetch of the rows of the maps that unit u's
-    // epilogue reads (one template per launch in these modes).
-    auto prefetch_maps = [&](int uu) {
-        const int g0 = (uu - (uu / ngroups) * ngroups) * C::RPB;
+    // Running-map modes: L2 prefetch of the rows of the maps that row group
+    // grp's epilogue reads (once per group: its templates follow one another).
+    auto prefetch_maps = [&](int grp) {
+        const int g0 = grp * C::RPB;
         for (int r = 0; r < C::RPB; ++r) {
             const int yy = g0 + r;
             if (yy >= out_rows) break;
@@ -763,16 +794,22 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
         }
     };
 
-    int u = blockIdx.x;
-    if (tid == 0 && u < units) issue(0, u);
-    if constexpr (MODE == kRunningMax || MODE == kRunningStats) {
-        if (tid == 0 && u < units) prefetch_maps(u);
+    int tj = 0, grp = 0;
+    bool have = unit_of(0, tj, grp);
+    if (tid == 0 && have) issue(0, tj, grp);
+    if constexpr (kRunning) {
+        if (tid == 0 && have) prefetch_maps(grp);
     }
     float pk_run = -INFINITY;  // kStorePeak: this warp's template pk_t so far
     int pk_t = -1;
-    for (int it = 0; u < units; ++it, u += gridDim.x) {
-        const int tj = u / ngroups, grp = u - tj * ngroups;
+    for (int it = 0; have; ++it) {
+        int next_tj = 0, next_grp = 0;
+        const bool more = unit_of(it + 1, next_tj, next_grp);
         float* outj = out + tj * out_tstride;
+        // Running modes: template j of this launch has index tindex + j, and
+        // only the launch's first template resets the maps.
+        [[maybe_unused]] const int reset_j = tj == 0 ? reset : 0;
+        [[maybe_unused]] const int index_j = tindex + tj;
         if constexpr (MODE == kStorePeak) {
             if (pk_t >= 0 && pk_t != tj) {  // block-uniform
                 fold_warp_peak(pk_run, peak + pk_t);
@@ -782,13 +819,12 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
         }
         const int b = it & 1;
         const uint32_t parity = (it >> 1) & 1;
-        const bool more = u + (int)gridDim.x < units;
-        if (tid == 0 && more) issue(b ^ 1, u + gridDim.x);
-        if constexpr (MODE == kRunningMax || MODE == kRunningStats) {
+        if (tid == 0 && more) issue(b ^ 1, next_tj, next_grp);
+        if constexpr (kRunning) {
             // The maps the NEXT group's epilogue reads: into L2 a whole
             // iteration ahead (whole 16-byte chunks inside each row only).
             // The first group's were requested before the loop.
-            if (tid == 0 && more) prefetch_maps(u + gridDim.x);
+            if (tid == 0 && more && next_grp != grp) prefetch_maps(next_grp);
         }
         const bool ok = mbar_wait_bounded(&mbar[b], parity);
         if (__syncthreads_or(!ok)) {  // block-uniform: every lane folds its warp
@@ -900,7 +936,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                         for (int i = 0; i < MCH; ++i) {
                             const int m = bb + (r0 + i) * NBL;
                             float2 c = c_make(-INFINITY, -INFINITY);
-                            if (!(reset & kResetMax)) {
+                            if (!(reset_j & kResetMax)) {
                                 if (rv && 2 * m + 1 < out_cols) {
                                     c = reinterpret_cast<const float2*>(orow)[m];
                                 } else {
@@ -915,27 +951,27 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                             const int m = bb + (r0 + i) * NBL;
                             const float2 z = v[q * RL + r0 + i];
                             const float2 c = cur[i];
-                            const bool rmax = (reset & kResetMax) != 0;
+                            const bool rmax = (reset_j & kResetMax) != 0;
                             const bool u0 = rmax || z.x > c.x, u1 = rmax || z.y > c.y;
                             if (rv && 2 * m + 1 < out_cols) {
                                 if (u0 && u1) {
                                     reinterpret_cast<float2*>(orow)[m] = z;
-                                    reinterpret_cast<int2*>(arow)[m] = make_int2(tindex, tindex);
+                                    reinterpret_cast<int2*>(arow)[m] = make_int2(index_j, index_j);
                                 } else if (u0) {
                                     orow[2 * m] = z.x;
-                                    arow[2 * m] = tindex;
+                                    arow[2 * m] = index_j;
                                 } else if (u1) {
                                     orow[2 * m + 1] = z.y;
-                                    arow[2 * m + 1] = tindex;
+                                    arow[2 * m + 1] = index_j;
                                 }
                             } else {
                                 if (u0 && 2 * m < out_cols) {
                                     orow[2 * m] = z.x;
-                                    arow[2 * m] = tindex;
+                                    arow[2 * m] = index_j;
                                 }
                                 if (u1 && 2 * m + 1 < out_cols) {
                                     orow[2 * m + 1] = z.y;
-                                    arow[2 * m + 1] = tindex;
+                                    arow[2 * m + 1] = index_j;
                                 }
                             }
                         }
@@ -947,7 +983,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                     float* srow = sum + (size_t)y * out_pitch;
                     float* qrow = sumsq + (size_t)y * out_pitch;
                     const bool rvs = aligned8(srow) && aligned8(qrow);
-                    const bool fresh = (reset & (kResetMax | kResetSums)) != 0;
+                    const bool fresh = (reset_j & (kResetMax | kResetSums)) != 0;
                     constexpr int SCH = largest_divisor_upto(RL, 4);
 #pragma unroll
                     for (int q = 0; q < I::bpt(I::S - 1); ++q) {
@@ -1004,6 +1040,9 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
         }
         // Rows past the end contribute -inf.
         if constexpr (MODE == kStorePeak) pk_run = fmax_nan(pk_run, pk);
+        tj = next_tj;
+        grp = next_grp;
+        have = more;
     }
     if constexpr (MODE == kStorePeak) {
         if (pk_t >= 0) fold_warp_peak(pk_run, peak + pk_t);

@@ -49,12 +49,18 @@ RESET_ALL = 1   # the batch's first template overwrites every map
 RESET_SUMS = 2  # ... overwrites the sum maps only
 
 
-def search_workspace_elems(H: int, W: int, h: int, chunk: int = 32) -> int:
-    """complex64 elements of a workspace holding the intermediate plus the row
-    spectra of `chunk` templates (the library then transforms the rows of up
-    to 32 templates per launch)."""
-    h_pad = (h + 1) // 2 * 2
-    return _lib.load().zfft_workspace_bytes(H, W) // 8 + chunk * (W // 2) * h_pad
+# Templates per launch of the search's kernels: the workspace holds this many
+# intermediate slices (1.07 GB at 4096^2), so the inverse row pass folds 16
+# templates into each row group of the maps while those map rows stay in L2,
+# and the column pass reads each spectrum column from DRAM once per 16.
+SEARCH_GROUP = 16
+
+
+def search_workspace_elems(H: int, W: int, h: int, group: int = SEARCH_GROUP) -> int:
+    """complex64 elements of a workspace of `group` intermediate slices (the
+    library then runs `group` templates through each kernel per launch)."""
+    del h  # the slices hold each template's row spectra too
+    return group * (_lib.load().zfft_workspace_bytes(H, W) // 8)
 
 
 def _cuda_workspace(H: int, W: int, h: int, device) -> torch.Tensor:
