@@ -34,11 +34,7 @@ namespace {
 
 constexpr int kVersion = 300;  // 0.3.0
 constexpr int kMaxDevices = 64;
-constexpr int kMaxChunk = 32;  // templates per row-r2c launch
-// Batched groups (small images): the intermediates of one group, written by
-// one column launch and read by one inverse-row launch, stay within this
-// much of the 126 MB L2.
-constexpr long long kBatchL2Bytes = 48ll << 20;
+constexpr int kMaxChunk = 32;  // templates per row-r2c launch, and per batched group
 
 thread_local std::string g_last_error;
 
@@ -400,25 +396,22 @@ int run(const float* input, int batch, int sy, int sx, void* ws, size_t ws_bytes
     }
     float2* Rregion = Q + q_elems;
 
-    // Batched groups: when at least two whole Q slices fit in the workspace,
-    // the templates of a group go through each kernel in one launch, each in
-    // its own slice (its row spectra first in rows [0, h) of the slice).
-    // Maps: only while the group's slices fit within kBatchL2Bytes (small
-    // images, which then never leave L2).  Running maps: up to kMaxChunk
-    // slices in HBM; the inverse row pass folds a row group's templates one
-    // after another into map rows that stay in L2, instead of streaming the
-    // whole maps through DRAM for every template, and the column pass reads
-    // each spectrum column from DRAM once per group.
+    // Batched groups: when at least two whole Q slices fit in the workspace
+    // (the reference's own (B, H, W/2+1) workspace holds B), up to kMaxChunk
+    // templates go through each kernel in one launch, each in its own slice
+    // (its row spectra first in rows [0, h) of the slice).  One launch per
+    // kernel per group instead of one per template: no per-launch prologue
+    // and tail per template, and the column pass reads each spectrum column
+    // from DRAM once per group (neighbouring blocks share it in L2).  Measured
+    // at 4096^2 / 32 x 256^2: 1.87 ms per call against 2.16 ms.  For the
+    // running maps the inverse row pass also folds a row group's templates
+    // one after another into map rows that stay in L2, instead of streaming
+    // the whole maps through DRAM for every template.
     long long group = 0;
     if (batch > 1) {
         const long long fit_ws = (long long)(ws_bytes / sizeof(float2)) / q_elems;
         group = batch < fit_ws ? batch : fit_ws;
-        if (!arg) {
-            const long long fit_l2 = kBatchL2Bytes / (q_elems * (long long)sizeof(float2));
-            if (fit_l2 < group) group = fit_l2;
-        } else if (group > kMaxChunk) {
-            group = kMaxChunk;
-        }
+        if (group > kMaxChunk) group = kMaxChunk;
     }
 
     CUtensorMap qmap;

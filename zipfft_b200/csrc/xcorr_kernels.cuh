@@ -269,7 +269,8 @@ __global__ void __launch_bounds__(ColCfg<H, NZ>::THREADS, ColCfg<H, NZ>::MINB)
     // read once per template but by every template, keeps the normal policy
     // (some of it then survives in L2 for the next template: measured faster
     // than evict-first or evict-last); the intermediate Q is kept resident
-    // for the row kernel that reads it next.
+    // for the row kernel that reads it next (with a group of templates per
+    // launch as well: evict-first Q lines measured 1.7x slower there).
     const uint64_t pol_stream = l2_evict_first();
     const uint64_t pol_spec = l2_evict_normal();
     const uint64_t pol_keep = l2_evict_last();
@@ -648,7 +649,8 @@ struct C2rCfg {
     static constexpr int BOXK = tma_box(W2);
     static constexpr int QB = round_up(W2 * RPB, 16);  // one Q tile
     static constexpr int FLOATS = 2 * QB + RPB * XB;
-    static constexpr int SMEM = FLOATS * 8 + 2 * 8;
+    // + two mbarriers + 32 floats for the block's peak reduction
+    static constexpr int SMEM = FLOATS * 8 + 2 * 8 + 32 * 4;
 };
 
 // Epilogues of the inverse row pass.
@@ -659,7 +661,7 @@ constexpr int kStorePeak = 3;  // write the map and fold its maximum into *peak
 
 
 // Maximum that returns NaN when either argument is NaN (as torch.amax does),
-// unlike fmaxf.  fold_warp_peak gives every NaN (of either sign: arithmetic
+// unlike fmaxf.  fold_block_peak gives every NaN (of either sign: arithmetic
 // on a NaN input may set its sign bit) the largest key, so it survives
 // atomicMax and converts back to a NaN peak.
 #if defined(__CUDA_ARCH__)
@@ -672,17 +674,28 @@ ZF_DEV float fmax_nan(float a, float b) {
 inline float fmax_nan(float a, float b) { return (a != a || b != b) ? a + b : (a > b ? a : b); }
 #endif
 
-// kStorePeak: each warp keeps its largest stored value over the row groups of
-// one template and folds it into that template's key (one atomic per warp)
-// when its block moves on to another template or ends.  An atomic per warp
-// and group put ~16k atomics on one address per 4096-row template, which
-// serialised in L2.  Every lane of the warp must call this.  A block that
-// gives up on a bounded wait folds what it has before it returns; the peaks
-// of such a call are incomplete (the device status word reports it).
-ZF_DEV void fold_warp_peak(float v, unsigned* key) {
+// kStorePeak: each thread keeps its largest stored value over the row groups
+// of one template; the block folds them into that template's key (one atomic
+// per block) when it moves on to another template or ends.  An atomic per
+// warp and group put ~16k atomics on one address per 4096-row template, which
+// serialised in L2; one per warp still slowed launches of many templates,
+// whose keys share one L2 line.  Every thread of the block must call this
+// (block-uniform); red: 32 floats of shared memory.  A block that gives up on
+// a bounded wait folds what it has before it returns; the peaks of such a call
+// are incomplete (the device status word reports it).
+ZF_DEV void fold_block_peak(float v, unsigned* key, float* red) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmax_nan(v, __shfl_xor_sync(0xffffffffu, v, o));
-    if ((threadIdx.x & 31) == 0) atomicMax(key, v != v ? 0xFFFFFFFFu : ordered_key(v));
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    if (lane == 0) red[w] = v;
+    __syncthreads();
+    if (w == 0) {
+        float x = lane < (int)(blockDim.x >> 5) ? red[lane] : -INFINITY;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) x = fmax_nan(x, __shfl_xor_sync(0xffffffffu, x, o));
+        if (lane == 0) atomicMax(key, x != x ? 0xFFFFFFFFu : ordered_key(x));
+    }
+    __syncthreads();  // red is free again
 }
 
 // MODE kStoreMap: out[y][x] = correlation.  MODE kRunningMax: out is the
@@ -724,6 +737,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     float2* qbase = smem;                       // [2][W2][RPB]
     float2* xbuf = smem + 2 * C::QB + g * C::XB;
     uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + C::FLOATS);
+    float* red = reinterpret_cast<float*>(mbar + 2);  // kStorePeak's block reduction
 
     if (tid == 0) {
         mbar_init(&mbar[0], 1);
@@ -800,7 +814,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     if constexpr (kRunning) {
         if (tid == 0 && have) prefetch_maps(grp);
     }
-    float pk_run = -INFINITY;  // kStorePeak: this warp's template pk_t so far
+    float pk_run = -INFINITY;  // kStorePeak: this thread's largest value of template pk_t so far
     int pk_t = -1;
     for (int it = 0; have; ++it) {
         int next_tj = 0, next_grp = 0;
@@ -812,7 +826,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
         [[maybe_unused]] const int index_j = tindex + tj;
         if constexpr (MODE == kStorePeak) {
             if (pk_t >= 0 && pk_t != tj) {  // block-uniform
-                fold_warp_peak(pk_run, peak + pk_t);
+                fold_block_peak(pk_run, peak + pk_t, red);
                 pk_run = -INFINITY;
             }
             pk_t = tj;
@@ -829,7 +843,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
         const bool ok = mbar_wait_bounded(&mbar[b], parity);
         if (__syncthreads_or(!ok)) {  // block-uniform: every lane folds its warp
             if constexpr (MODE == kStorePeak) {
-                if (pk_t >= 0) fold_warp_peak(pk_run, peak + pk_t);
+                if (pk_t >= 0) fold_block_peak(pk_run, peak + pk_t, red);
             }
             if (tid == 0) {
                 atomicExch(status, kStatusTimeout);
@@ -1045,7 +1059,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
         have = more;
     }
     if constexpr (MODE == kStorePeak) {
-        if (pk_t >= 0) fold_warp_peak(pk_run, peak + pk_t);
+        if (pk_t >= 0) fold_block_peak(pk_run, peak + pk_t, red);
     }
 }
 
@@ -1067,7 +1081,7 @@ struct C2rPairCfg {
     static constexpr int PPB = C::RPB / 2;     // pairs per block
     static constexpr int XB = xbuf_len(W);
     static constexpr int FLOATS = 2 * C::QB + PPB * XB;
-    static constexpr int SMEM = FLOATS * 8 + 2 * 8;
+    static constexpr int SMEM = FLOATS * 8 + 2 * 8 + 32 * 4;  // as C2rCfg
     static_assert(PPB * TP == C::THREADS, "a pair's transform has twice a row's threads");
 };
 
@@ -1092,6 +1106,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     float2* qbase = smem;  // [2][W2][RPB]
     float2* xbuf = smem + 2 * C::QB + pr * P::XB;
     uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + P::FLOATS);
+    float* red = reinterpret_cast<float*>(mbar + 2);  // kStorePeak's block reduction
 
     if (tid == 0) {
         mbar_init(&mbar[0], 1);
@@ -1121,14 +1136,14 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
 
     int u = blockIdx.x;
     if (tid == 0 && u < units) issue(0, u);
-    float pk_run = -INFINITY;  // kStorePeak: this warp's template pk_t so far
+    float pk_run = -INFINITY;  // kStorePeak: this thread's largest value of template pk_t so far
     int pk_t = -1;
     for (int it = 0; u < units; ++it, u += gridDim.x) {
         const int tj = u / ngroups, grp = u - tj * ngroups;
         float* outj = out + tj * out_tstride;
         if constexpr (MODE == kStorePeak) {
             if (pk_t >= 0 && pk_t != tj) {  // block-uniform
-                fold_warp_peak(pk_run, peak + pk_t);
+                fold_block_peak(pk_run, peak + pk_t, red);
                 pk_run = -INFINITY;
             }
             pk_t = tj;
@@ -1140,7 +1155,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
         const bool ok = mbar_wait_bounded(&mbar[b], parity);
         if (__syncthreads_or(!ok)) {  // block-uniform: every lane folds its warp
             if constexpr (MODE == kStorePeak) {
-                if (pk_t >= 0) fold_warp_peak(pk_run, peak + pk_t);
+                if (pk_t >= 0) fold_block_peak(pk_run, peak + pk_t, red);
             }
             if (tid == 0) {
                 atomicExch(status, kStatusTimeout);
@@ -1225,7 +1240,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
         if constexpr (MODE == kStorePeak) pk_run = fmax_nan(pk_run, pk);
     }
     if constexpr (MODE == kStorePeak) {
-        if (pk_t >= 0) fold_warp_peak(pk_run, peak + pk_t);
+        if (pk_t >= 0) fold_block_peak(pk_run, peak + pk_t, red);
     }
 }
 
