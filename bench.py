@@ -45,8 +45,9 @@ TH = TW = 256
 BATCH = 32
 # Minimum bytes per correlation: fp32 template + c64 image spectrum + fp32 output.
 ALG_BYTES = TH * TW * 4 + H * (W // 2 + 1) * 8 + H * W * 4  # 134,512,640
-L2_NOTE = ("no L2 flush: every step streams 32 x 67 MB of spectrum reads and "
-           "2.1 GB of output writes through the 126 MB L2")
+L2_NOTE = ("no L2 flush: every step writes and reads back 2.1 GB of intermediates and "
+           "writes 2.1 GB of maps, through the 126 MB L2 (the 67 MB spectrum is read "
+           "by all 32 templates of the step's one column launch)")
 WORKLOAD = ("4096^2 f32 image (spectrum precomputed) x 32 soft-masked 256^2 f32 templates "
             "per GPU, full 4096^2 maps")
 

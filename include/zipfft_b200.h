@@ -45,8 +45,9 @@ extern "C" {
  *   fft_workspace complex64 scratch, 16-byte aligned; at least
  *                 zfft_workspace_bytes(fft_y, fft_x) bytes (one
  *                 (fft_y, fft_x/2 + 1) slice, as in the reference, is always
- *                 enough; the reference's (batch, fft_y, fft_x/2 + 1) lets the
- *                 row transforms of up to 32 templates run per launch).
+ *                 enough; the reference's (batch, fft_y, fft_x/2 + 1) holds
+ *                 one slice per template, and up to 32 templates then go
+ *                 through each kernel per launch -- the fast choice).
  *                 Clobbered.
  *   conv_data     complex64 [fft_x/2 + 1][fft_y], 16-byte aligned: rfft2 of the
  *                 image, transposed (the reference's pre-transposed layout,
@@ -150,7 +151,8 @@ ZFFT_API int zfft_padded_real_corr_2d_noalloc(const float* input, int batch, int
 /* Bytes of fft_workspace that zfft_padded_real_corr_2d, _conv_2d, _corr_2d_max,
  * _corr_2d_peaks and _corr_2d_max_stats need for an (fft_y, fft_x) image:
  * fft_y * (fft_x / 2) complex64 values, independent of the batch (templates
- * are processed one after another through the same slice).
+ * then go one after another through the same slice; each further whole slice
+ * lets one more template share the launches, up to 32).
  * Returns 0 for unsupported sizes.  No counterpart in the reference, which
  * sizes the workspace (batch, fft_y, fft_x/2 + 1) (binding.cu:235-245). */
 ZFFT_API size_t zfft_workspace_bytes(int fft_size_y, int fft_size_x);
