@@ -92,10 +92,11 @@ def test_corr_max_stats_match_oracle(B, h, w, H, W, full):
 
 
 def test_search_stats_over_1024_templates_match_float64_sums():
-    """stats=True over 1024 templates in 4 batches of 256: the kernels sum each
-    batch in float32 and the search adds the batches in float64, so the
-    per-pixel sums stay within the batch's rounding of the oracle's float64
-    sums (naive float32 accumulation over all 1024 would not)."""
+    """stats=True over 1024 templates from host memory in batches of up to
+    256 (the first ones ramped up from 16): the kernels sum each batch in
+    float32 and the search adds the batches in float64, so the per-pixel sums
+    stay within the batch's rounding of the oracle's float64 sums (naive
+    float32 accumulation over all 1024 would not)."""
     from zipfft_b200.search import template_search
 
     H = W = 256

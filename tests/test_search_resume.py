@@ -159,3 +159,27 @@ def test_stats_search_resumes_with_its_sums(tmp_path):
     _search(tm, spec, checkpoint_every=2, on_checkpoint=plain.append)
     with pytest.raises(ValueError, match="no sum maps"):
         _search(tm, spec, stats=True, resume=plain[0])
+
+
+def test_batch_bounds_ramp_covers_the_shard_in_order():
+    """Host-resident templates: the first batches ramp up from the launch
+    group size, doubling up to the batch size; the ranges tile the shard."""
+    from zipfft_b200.search import SEARCH_GROUP, batch_bounds
+
+    for start, stop, nb in [(0, 1024, 256), (5, 1000, 256), (0, 7, 256), (3, 40, 8), (0, 0, 4)]:
+        plain = list(batch_bounds(start, stop, nb))
+        ramp = list(batch_bounds(start, stop, nb, ramp=True))
+        for bounds in (plain, ramp):
+            if not bounds:
+                assert start == stop
+                continue
+            assert [b[0] for b in bounds] == [start] + [b[1] for b in bounds[:-1]]
+            assert bounds[-1][1] == stop
+            assert all(0 < b1 - b0 <= nb for b0, b1 in bounds)
+        assert all(b1 - b0 == nb for b0, b1 in plain[:-1])
+        if ramp:
+            sizes = [b1 - b0 for b0, b1 in ramp]
+            assert sizes[0] == min(nb, SEARCH_GROUP, stop - start)
+            assert all(b <= min(2 * a, nb) for a, b in zip(sizes, sizes[1:]))
+    assert [b1 - b0 for b0, b1 in batch_bounds(0, 1024, 256, ramp=True)] == \
+        [16, 32, 64, 128, 256, 256, 256, 16]

@@ -63,6 +63,22 @@ def search_workspace_elems(H: int, W: int, h: int, group: int = SEARCH_GROUP) ->
     return group * (_lib.load().zfft_workspace_bytes(H, W) // 8)
 
 
+def batch_bounds(start: int, stop: int, nb: int, ramp: bool = False):
+    """The [b0, b1) template ranges of a shard, batches of nb.  ramp: the
+    first batches grow from SEARCH_GROUP templates, doubling up to nb, so
+    that the first copy from host memory is small and each later copy
+    overlaps the computation of the batch before it (with eight ranks
+    sharing the host's copy bandwidth, a first batch of 256 templates of
+    384^2 took 6.6 ms to arrive, against 0.4 ms for 16)."""
+    size = min(nb, SEARCH_GROUP) if ramp else nb
+    b0 = start
+    while b0 < stop:
+        b1 = min(b0 + size, stop)
+        yield b0, b1
+        b0 = b1
+        size = min(2 * size, nb)
+
+
 def _cuda_workspace(H: int, W: int, h: int, device) -> torch.Tensor:
     return torch.empty(search_workspace_elems(H, W, h), dtype=torch.complex64, device=device)
 
@@ -260,8 +276,7 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
     mark("start")
     # A resumed shard has maps to fold into; a fresh one starts by overwriting.
     first = start == lo
-    for j, b0 in enumerate(range(start, hi, nb)):
-        b1 = min(b0 + nb, hi)
+    for j, (b0, b1) in enumerate(batch_bounds(start, hi, nb, ramp=on_host)):
         batch = stage(j % 2, b0, b1)
         if j == 0:
             mark("first_copy")
