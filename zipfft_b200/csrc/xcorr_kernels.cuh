@@ -25,7 +25,9 @@
 // rows [0, h) of the same slice (pitch H; the column kernel then overwrites it
 // in place, each column by the block that read it) or in a separate region
 // with pitch round_up(h, 2) so that the row kernel can run several templates
-// per launch.
+// per launch.  With a workspace of several slices (batched groups), each
+// kernel runs a group of templates per launch, template j in slice j with its
+// R in rows [0, h) of that slice.
 //
 // Differences from the reference's data movement (io.hpp:134-195, which reads
 // a row-major workspace down its columns at stride W/2+1):
