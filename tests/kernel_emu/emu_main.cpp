@@ -137,78 +137,6 @@ inline T __ldg(const T* p) {
 
 float2* zf::dyn_smem() { return emu_smem; }
 
-// Named barriers (bar.sync / bar.arrive / bar.red.or with an id and a thread
-// count).  Every lane of a warp must execute the same barrier instruction
-// (they are .aligned): the lanes meet at the warp's rendezvous and compare
-// call sites and arguments first.  Each id's barrier is created per block
-// with the count of its first use, later uses must give the same count, and
-// when a block ends every id must have completed all its phases (an arrival
-// without its matching waits, as an unbalanced token hand-off would leave,
-// aborts the run).
-struct EmuNamedBar {
-    std::unique_ptr<std::barrier<>> bar;
-    unsigned count = 0;
-    std::atomic<unsigned long long> arrivals{0};
-    std::atomic<int> flag[2];
-};
-thread_local EmuNamedBar* emu_named = nullptr;  // [16], per block
-thread_local unsigned emu_named_calls[16];      // this thread's or-calls per id
-static std::mutex emu_named_mu;
-thread_local void** emu_warp_sites = nullptr;   // [32] per warp
-static void emu_warp_agree(void* site, unsigned id, unsigned count) {
-    const unsigned lane = threadIdx.x & 31u;
-    const uintptr_t key = reinterpret_cast<uintptr_t>(site) ^ (uintptr_t(id) << 48) ^ (uintptr_t(count) << 32);
-    emu_warp_sites[lane] = reinterpret_cast<void*>(key);
-    emu_warp_bar->arrive_and_wait();
-    const unsigned w0 = threadIdx.x & ~31u;
-    for (unsigned l = 0; l < 32 && w0 + l < blockDim.x; ++l) {
-        if (emu_warp_sites[l] != reinterpret_cast<void*>(key)) {
-            std::fprintf(stderr, "divergent named barrier %u in warp %u\n", id, w0 / 32);
-            std::abort();
-        }
-    }
-    emu_warp_bar->arrive_and_wait();
-}
-static EmuNamedBar& emu_named_get(unsigned id, unsigned count) {
-    if (id == 0 || id >= 16 || count == 0 || count % 32 || count > blockDim.x) {
-        std::fprintf(stderr, "bad named barrier id %u count %u\n", id, count);
-        std::abort();
-    }
-    std::lock_guard<std::mutex> l(emu_named_mu);
-    EmuNamedBar& b = emu_named[id];
-    if (!b.bar) {
-        b.bar = std::make_unique<std::barrier<>>(count);
-        b.count = count;
-    } else if (b.count != count) {
-        std::fprintf(stderr, "named barrier %u used with counts %u and %u\n", id, b.count, count);
-        std::abort();
-    }
-    return b;
-}
-__attribute__((noinline)) void zf::named_barrier_sync(uint32_t id, uint32_t count) {
-    emu_warp_agree(__builtin_return_address(0), id, count);
-    EmuNamedBar& b = emu_named_get(id, count);
-    b.arrivals.fetch_add(1);
-    b.bar->arrive_and_wait();
-}
-__attribute__((noinline)) void zf::named_barrier_arrive(uint32_t id, uint32_t count) {
-    emu_warp_agree(__builtin_return_address(0), id, count);
-    EmuNamedBar& b = emu_named_get(id, count);
-    b.arrivals.fetch_add(1);
-    (void)b.bar->arrive();
-}
-__attribute__((noinline)) bool zf::named_barrier_or(uint32_t id, uint32_t count, bool pred) {
-    emu_warp_agree(__builtin_return_address(0), id, count);
-    EmuNamedBar& b = emu_named_get(id, count);
-    const unsigned slot = emu_named_calls[id]++ & 1u;
-    if (pred) b.flag[slot].store(1);
-    b.arrivals.fetch_add(2);
-    b.bar->arrive_and_wait();
-    const bool r = b.flag[slot].load() != 0;
-    b.bar->arrive_and_wait();  // everyone has read the flag
-    b.flag[slot].store(0);
-    return r;
-}
 
 // mbarrier stand-in: phase parity, pending arrivals, transaction bytes.
 struct EmuBar {
@@ -368,8 +296,6 @@ void emu_launch(dim3 grid, int block, size_t smem_bytes, K kernel, A... args) {
     for (int w = 0; w < nwarps; ++w)
         wbars.push_back(std::make_unique<std::barrier<>>(std::min(32, block - 32 * w)));
     std::vector<float> wbuf((size_t)nwarps * 32);
-    std::vector<void*> wsites((size_t)nwarps * 32);
-    std::vector<EmuNamedBar> named(16);
     std::vector<std::thread> threads;
     for (int tid = 0; tid < block; ++tid) {
         threads.emplace_back([&, tid] {
@@ -384,13 +310,10 @@ void emu_launch(dim3 grid, int block, size_t smem_bytes, K kernel, A... args) {
             emu_sites = sites;
             emu_warp_bar = wbars[tid / 32].get();
             emu_warp_buf = wbuf.data() + (tid / 32) * 32;
-            emu_warp_sites = wsites.data() + (tid / 32) * 32;
-            emu_named = named.data();
             for (unsigned by = 0; by < grid.y; ++by) {
                 for (unsigned bx = 0; bx < grid.x; ++bx) {
                     blockIdx.x = bx;
                     blockIdx.y = by;
-                    for (auto& c : emu_named_calls) c = 0;
                     kernel(args...);
                     if (!emu_pending_stores.empty()) {
                         std::fprintf(stderr, "block %u exited with %zu bulk store(s) not waited "
@@ -403,23 +326,6 @@ void emu_launch(dim3 grid, int block, size_t smem_bytes, K kernel, A... args) {
                         std::fprintf(stderr, "block %u exited with %zu TMA load(s) in flight\n",
                                      bx, emu_pending_load_count());
                         std::abort();
-                    }
-                    if (tid == 0) {  // every named barrier ended on a completed phase
-                        for (unsigned id = 0; id < 16; ++id) {
-                            EmuNamedBar& nb = named[id];
-                            if (nb.bar && nb.arrivals.load() % nb.count != 0) {
-                                std::fprintf(stderr, "block %u ended with named barrier %u "
-                                                     "part-way through a phase (%llu arrivals, "
-                                                     "count %u)\n",
-                                             bx, id, nb.arrivals.load(), nb.count);
-                                std::abort();
-                            }
-                            // a fresh barrier for the next block
-                            nb.bar.reset();
-                            nb.count = 0;
-                            nb.arrivals = 0;
-                            nb.flag[0] = nb.flag[1] = 0;
-                        }
                     }
                     bar.arrive_and_wait();  // the check precedes the next block's loads
                 }

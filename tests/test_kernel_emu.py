@@ -106,7 +106,7 @@ CASES = [
     (4, 30, 30, 256, 256, True, True, 2, 2, 4),
     (2, 100, 20, 2048, 64, True, True, 1, None, 2),   # one column per block: bulk column stores
     (1, 129, 9, 2048, 64, False, False, 2, None, 0),  # valid crop, odd store length
-    (2, 10, 100, 64, 2048, True, True, None, None, 2),  # rows on their own warps, named barriers
+    (2, 10, 100, 64, 2048, True, True, None, None, 2),  # wide rows (W/2 = 1024), chunked
     (1, 33, 300, 128, 2048, False, False, None, None, 0),
 ]
 

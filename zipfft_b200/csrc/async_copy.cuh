@@ -162,36 +162,7 @@ ZF_DEV void l2_discard_line(const void* p) {
 
 ZF_DEV long long cycle_clock() { return clock64(); }
 
-// Named CTA barriers (ids 1..15; id 0 is __syncthreads).  `count` threads
-// (a multiple of 32) take part in each phase; every thread of a warp executes
-// the same barrier instruction.  sync waits for the phase; arrive counts this
-// warp in without waiting (the producer side of a hand-off); or_sync waits and
-// returns whether any participant passed pred = true.  Like __syncthreads,
-// sync and or_sync order the participants' shared-memory accesses.
-ZF_DEV void named_barrier_sync(uint32_t id, uint32_t count) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-ZF_DEV void named_barrier_arrive(uint32_t id, uint32_t count) {
-    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-ZF_DEV bool named_barrier_or(uint32_t id, uint32_t count, bool pred) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.ne.u32 p, %1, 0;\n\t"
-        "bar.red.or.pred q, %2, %3, p;\n\t"
-        "selp.u32 %0, 1, 0, q;\n\t}"
-        : "=r"(r)
-        : "r"(pred ? 1u : 0u), "r"(id), "r"(count)
-        : "memory");
-    return r != 0;
-}
-
 #else  // host stand-ins for the CPU test harness -------------------------------
-
-void named_barrier_sync(uint32_t id, uint32_t count);
-void named_barrier_arrive(uint32_t id, uint32_t count);
-bool named_barrier_or(uint32_t id, uint32_t count, bool pred);
 
 struct CUtensorMap {  // what the harness needs of a 2D tiled tensor map
     const unsigned char* base;
