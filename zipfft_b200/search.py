@@ -188,6 +188,10 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
     its own templates), its first template having global index shard_base;
     nothing is split further.  The ranks' shards must not overlap.
 
+    Device memory: the maps, two template batches (from host memory), and a
+    workspace of SEARCH_GROUP intermediate slices (16 x H x W/2 complex64,
+    1.07 GB at 4096^2), so that 16 templates share each kernel launch.
+
     phase_events: a dict that receives timing events recorded on the compute
     stream at each phase boundary ("start", "first_copy" (the first batch is
     on the device), "batches", "pack", "reduce", "unpack", "end"; the last
