@@ -206,10 +206,10 @@ def test_bounded_wait_reports_timeout_and_context_survives():
 
 @pytest.mark.parametrize("H,h,B", [(4096, 256, 5), (1024, 100, 7), (3840, 384, 3)])
 def test_chunked_and_in_place_layouts_agree(H, h, B):
-    """Workspaces large enough for several templates' rows (chunked row
-    launches) or, for small images, several whole intermediates (batched
-    groups: one launch per kernel for a group of templates) give bit-identical
-    results to the minimal in-place workspace."""
+    """A workspace of several whole intermediates (batched groups: one launch
+    per kernel for up to 32 templates) gives bit-identical results to the
+    minimal in-place workspace (one template per column and inverse-row
+    launch)."""
     from zipfft_b200 import _lib
 
     _, tm, spec = make_inputs(B, h, h, H, H, seed=H + B)
