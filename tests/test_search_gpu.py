@@ -264,27 +264,25 @@ def test_search_two_gpus_nccl(tmp_path):
                                                   (7, 40, 30, 1024, 512, False, True),
                                                   (4, 384, 384, 3840, 3840, True, True)])
 def test_grouped_running_maps_equal_per_template_launches(B, h, w, H, W, full, stats):
-    """corr_max with a (B, H, W/2+1) workspace runs the templates as one
-    batched group (each block folds a row group's templates in order); the
-    maps, argmax and sums equal the one-slice workspace's per-template
+    """The running-map call with a workspace of B slices runs the templates as
+    one batched group (each block folds a row group's templates in order);
+    the maps, argmax and sums equal the one-slice workspace's per-template
     launches bit for bit."""
-    import zipfft
     from zipfft_b200 import _lib
+    from zipfft_b200.search import RESET_ALL, _cuda_corr_max
 
     _, tm, spec = make_inputs(B, h, w, H, W, seed=B + h)
     dev = torch.device("cuda", 0)
     oy, ox = O.out_shape(h, w, H, W, full)
     res = []
-    for ws in (torch.empty(_lib.load().zfft_workspace_bytes(H, W) // 8, dtype=torch.complex64,
-                           device=dev),
-               torch.empty((B, H, W // 2 + 1), dtype=torch.complex64, device=dev)):
+    slice_elems = _lib.load().zfft_workspace_bytes(H, W) // 8
+    for slices in (1, B):  # through the C ABI, which takes any workspace size
+        ws = torch.empty(slices * slice_elems, dtype=torch.complex64, device=dev)
         mx = torch.empty((oy, ox), device=dev)
         am = torch.empty((oy, ox), dtype=torch.int32, device=dev)
         sm = torch.empty((oy, ox), device=dev) if stats else None
         sq = torch.empty((oy, ox), device=dev) if stats else None
-        zipfft.padded_rconv2d.corr_max(tm.to(dev), ws, spec.to(dev), mx, am, H, W,
-                                       template_index_base=3, reset=True, sum_map=sm,
-                                       sumsq_map=sq)
+        _cuda_corr_max(tm.to(dev), ws, spec.to(dev), mx, am, H, W, 3, RESET_ALL, sm, sq)
         torch.cuda.synchronize()
         res.append([t.cpu() for t in (mx, am, sm, sq) if t is not None])
     for a, b in zip(*res):
