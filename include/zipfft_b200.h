@@ -108,8 +108,11 @@ ZFFT_API int zfft_padded_real_corr_2d_max(const float* input, int batch, int sig
  * with.  reset: 0 folds every template into all four maps; 1 lets the first
  * template overwrite all four; 2 lets it overwrite the two sum maps only (the
  * maximum and argmax keep folding), so that a long search can sum each batch
- * in float32 and add the batches up at higher precision.  No counterpart in
- * the reference (README.md:24 motivates the use). */
+ * in float32 and add the batches up at higher precision.  sum_map may be
+ * NULL: the sum of squares alone is accumulated (the sum of a batch's maps is
+ * also the map of the batch's summed template, correlation being linear, one
+ * zfft_padded_real_corr_2d call).  No counterpart in the reference
+ * (README.md:24 motivates the use). */
 ZFFT_API int zfft_padded_real_corr_2d_max_stats(const float* input, int batch, int signal_y,
                                                 int signal_x, void* fft_workspace,
                                                 size_t fft_workspace_bytes, const void* conv_data,

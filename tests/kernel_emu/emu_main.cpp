@@ -413,6 +413,10 @@ void run_c2r(const float2* Q, int H, float* out, int* arg, float* sum, float* su
         emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM,
                    zf::k_row_c2r<W2, zf::kRunningStats>, map, out, arg, sum, sumsq, np, tw, ttr.data(), orows,
                    ocols, ocols, tindex, reset, nt, ots, &g_status);
+    else if (arg && sumsq)
+        emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM,
+                   zf::k_row_c2r<W2, zf::kRunningSumSq>, map, out, arg, nf, sumsq, np, tw, ttr.data(), orows,
+                   ocols, ocols, tindex, reset, nt, ots, &g_status);
     else if (arg)
         emu_launch(dim3{(unsigned)grid, 1, 1}, C::THREADS, C::SMEM, zf::k_row_c2r<W2, zf::kRunningMax>,
                    map, out, arg, nf, nf, np, tw, ttr.data(), orows, ocols, ocols, tindex, reset, nt, ots,
@@ -535,8 +539,9 @@ int main(int argc, char** argv) {
     const int B = hd[0], sy = hd[1], sx = hd[2], H = hd[3], W = hd[4], oy = hd[5], ox = hd[6];
     const bool conj = hd[7] != 0;
     const int cap = hd[8], nz_col = hd[9], nz_row = hd[10], chunk = hd[11];
-    const bool max_mode = hd[12] == 1 || hd[12] == 2;  // fold into running max / argmax maps
-    const bool stats = hd[12] == 2;                    // ... and into sum / sum-of-squares maps
+    const bool max_mode = hd[12] == 1 || hd[12] == 2 || hd[12] == 4;  // running max / argmax maps
+    const bool stats = hd[12] == 2 || hd[12] == 4;  // ... and sum (not with 4) / sum-of-squares maps
+    const bool no_sum = hd[12] == 4;                // the sum of squares alone (sum stays 0)
     const bool peaks_mode = hd[12] == 3;               // maps plus per-template peaks
     const int group = hd[13] & 0xFFFF;                   // >= 2: batched groups
     const bool poison = (hd[13] >> 16) & 1;              // workspace starts as NaN
@@ -568,7 +573,7 @@ int main(int argc, char** argv) {
     std::vector<float> out((size_t)(max_mode ? 1 : B) * oy * ox);
     std::vector<int> arg(max_mode ? (size_t)oy * ox : 0);
     std::vector<float> sum(stats ? (size_t)oy * ox : 0), sumsq(stats ? (size_t)oy * ox : 0);
-    float* sum_p = stats ? sum.data() : nullptr;
+    float* sum_p = stats && !no_sum ? sum.data() : nullptr;
     float* sumsq_p = stats ? sumsq.data() : nullptr;
     std::vector<unsigned> peak_keys(peaks_mode ? B : 0, 0u);
     auto twH = twiddles(H), twW = twiddles(W);

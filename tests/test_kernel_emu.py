@@ -70,12 +70,12 @@ def run_emu(exe, tmp_path, B, sy, sx, H, W, conj, full, nz_col=None, nz_row=None
     res = subprocess.run([exe, fin, fout], capture_output=True, text=True)
     assert res.returncode == 0, res.stderr[-4000:]
     ref = O.padded_corr2d_f64(tm, spec, H, W, conj, full)
-    if max_mode in (1, 2):  # True counts as 1
+    if max_mode in (1, 2, 4):  # True counts as 1; 4: sum of squares without the sum
         raw = np.fromfile(fout, np.uint8)
         n = oy * ox * 4
         mx = raw[:n].view(np.float32).reshape(oy, ox)
         am = raw[n:2 * n].view(np.int32).reshape(oy, ox)
-        if max_mode == 2:
+        if max_mode in (2, 4):
             sm = raw[2 * n:3 * n].view(np.float32).reshape(oy, ox)
             sq = raw[3 * n:4 * n].view(np.float32).reshape(oy, ox)
             return (mx, am, sm, sq), ref
@@ -321,3 +321,17 @@ def test_emulated_grouped_running_maps(emu, tmp_path, group, W, full, sx, max_mo
     # the same per-pixel arithmetic in the same template order: bit-identical
     for a, b in zip(got, one):
         assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("group", [0, 3])
+def test_emulated_sum_of_squares_without_sum(emu, tmp_path, group):
+    """kRunningSumSq: the maximum, argmax and sum of squares as kRunningStats
+    computes them (bit for bit), no sum map written."""
+    B, H, W = 5, 64, 128
+    (mx, am, sm, sq), ref = run_emu(emu, tmp_path, B, 12, 9, H, W, True, False, max_mode=4,
+                                    group=group)
+    (mx2, am2, sm2, sq2), _ = run_emu(emu, tmp_path, B, 12, 9, H, W, True, False, max_mode=2,
+                                      group=group)
+    assert np.array_equal(mx, mx2) and np.array_equal(am, am2) and np.array_equal(sq, sq2)
+    assert not sm.any()
+    assert O.rel_l2((ref ** 2).sum(axis=0), sq) < 1e-5

@@ -290,3 +290,41 @@ def test_grouped_running_maps_equal_per_template_launches(B, h, w, H, W, full, s
     ref = O.padded_corr2d_f64(tm.numpy(), spec.numpy(), H, W, True, full)
     assert O.rel_l2(ref.max(axis=0), res[1][0].numpy()) < 5e-6
     assert int(res[1][1].min()) >= 3 and int(res[1][1].max()) < 3 + B
+
+
+def test_max_stats_without_sum_map_matches_with_it():
+    """zfft_padded_real_corr_2d_max_stats with sum_map NULL accumulates the
+    maximum, argmax and sum of squares exactly as with a sum map (bit for
+    bit); the search's sum map, taken as the correlation map of each batch's
+    summed template, matches the oracle's float64 sums."""
+    from zipfft_b200 import _lib
+
+    B, h, w, H, W = 6, 40, 30, 512, 256
+    _, tm, spec = make_inputs(B, h, w, H, W, seed=77)
+    dev = torch.device("cuda", 0)
+    lib = _lib.load()
+    ws = torch.empty(B * lib.zfft_workspace_bytes(H, W) // 8, dtype=torch.complex64, device=dev)
+    stream = torch.cuda.current_stream(0).cuda_stream
+    out = []
+    for with_sum in (True, False):
+        mx = torch.empty((H, W), device=dev)
+        am = torch.empty((H, W), dtype=torch.int32, device=dev)
+        sm = torch.zeros((H, W), device=dev)
+        sq = torch.empty((H, W), device=dev)
+        _lib.check(lib.zfft_padded_real_corr_2d_max_stats(
+            tm.to(dev).data_ptr(), B, h, w, ws.data_ptr(), ws.numel() * 8, spec.to(dev).data_ptr(),
+            mx.data_ptr(), am.data_ptr(), sm.data_ptr() if with_sum else None, sq.data_ptr(),
+            H, W, H, W, 0, 1, 0, stream))
+        torch.cuda.synchronize()
+        out.append((mx.cpu(), am.cpu(), sq.cpu(), sm.cpu()))
+    for a, b in zip(out[0][:3], out[1][:3]):
+        assert torch.equal(a, b)
+    assert not out[1][3].any()  # no sum map: nothing written to the untouched buffer
+
+    from zipfft_b200.search import template_search
+
+    mx, am, sm, sq = template_search(tm, spec.to(dev), H, W, batch_size=4, full=True, stats=True)
+    ref = O.padded_corr2d_f64(tm.numpy(), spec.numpy(), H, W, True, True)
+    scale = np.sqrt((ref ** 2).sum(axis=0).max())
+    assert np.abs(sm.cpu().numpy() - ref.sum(axis=0)).max() / scale < 1e-5
+    assert O.rel_l2((ref ** 2).sum(axis=0), sq.cpu().numpy()) < 5e-6

@@ -740,8 +740,8 @@ int zfft_padded_real_corr_2d_max_stats(const float* input, int batch, int signal
                                        float* sumsq_map, int output_y, int output_x,
                                        int fft_size_y, int fft_size_x, int template_index_base,
                                        int reset, int device, void* stream) {
-    if ((!arg_map || !sum_map || !sumsq_map) && batch > 0)
-        return fail(ZFFT_ERROR_INVALID_VALUE, "null argmax, sum or sum-of-squares map");
+    if ((!arg_map || !sumsq_map) && batch > 0)
+        return fail(ZFFT_ERROR_INVALID_VALUE, "null argmax or sum-of-squares map");
     if (template_index_base < 0 || (long long)template_index_base + batch > 0x7FFFFFFFLL)
         return fail(ZFFT_ERROR_INVALID_VALUE, "template indices must lie in [0, 2^31 - 1)");
     if (reset < 0 || reset > 2)

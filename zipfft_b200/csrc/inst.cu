@@ -168,8 +168,8 @@ cudaError_t c2r_t(const CUtensorMap* qmap, float* out, int* arg, float* sum, flo
     // The running-map modes hand each block whole row groups (all of the
     // launch's templates for each), the map modes (template, group) units.
     const long long groups = (out_rows + C::RPB - 1) / C::RPB;
-    const long long units = (MODE == kRunningMax || MODE == kRunningStats) ? groups
-                                                                           : groups * ntemplates;
+    constexpr bool kRunning = MODE == kRunningMax || MODE == kRunningStats || MODE == kRunningSumSq;
+    const long long units = kRunning ? groups : groups * ntemplates;
     const int grid = (int)(units < cap ? units : cap);
     // The peaks epilogue over a group of templates is launched without
     // programmatic serialization: with it, the launch ran 1.2-1.4x longer and
@@ -277,8 +277,12 @@ cudaError_t ZF_CAT(launch_row_c2r_, ZF_SIZE)(const CUtensorMap* qmap, float* out
     if (ntemplates < 1) return cudaErrorInvalidValue;
     // Running maps: ntemplates consecutive templates (indices tindex, ...)
     // folded into the same maps (out_tstride unused).
-    if (arg != nullptr && sum != nullptr)
+    if (arg != nullptr && sum != nullptr && sumsq != nullptr)
         return c2r_t<W2, kRunningStats>(qmap, out, arg, sum, sumsq, nullptr, tw, out_rows,
+                                        out_cols, out_pitch, tindex, reset, ntemplates, 0, status,
+                                        device, s);
+    if (arg != nullptr && sumsq != nullptr)  // the sum of squares alone
+        return c2r_t<W2, kRunningSumSq>(qmap, out, arg, nullptr, sumsq, nullptr, tw, out_rows,
                                         out_cols, out_pitch, tindex, reset, ntemplates, 0, status,
                                         device, s);
     if (arg != nullptr)

@@ -660,6 +660,7 @@ constexpr int kStoreMap = 0;  // write the correlation map
 constexpr int kRunningMax = 1;  // fold it into a running per-pixel max / argmax
 constexpr int kRunningStats = 2;  // ... and into per-pixel sum and sum of squares
 constexpr int kStorePeak = 3;  // write the map and fold its maximum into *peak
+constexpr int kRunningSumSq = 4;  // as kRunningStats without the sum (sum of squares only)
 
 
 // Maximum that returns NaN when either argument is NaN (as torch.amax does),
@@ -709,7 +710,8 @@ ZF_DEV void fold_block_peak(float v, unsigned* key, float* red) {
 // correlation and its square are also added to the maps sum and sumsq (same
 // pitch; reset & (kResetMax | kResetSums) overwrites them instead, so that a
 // caller can start float32 partial sums per batch and accumulate the batches
-// at higher precision while the maximum keeps running).
+// at higher precision while the maximum keeps running).  MODE kRunningSumSq:
+// as kRunningStats without the sum map (sum unused).
 //
 // Several templates per launch: in the map modes the units (template, row
 // group) are strided over the grid.  In the running-map modes each block owns
@@ -765,7 +767,7 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
     // Units (template, row group): template j's Q is columns [j W2, (j+1) W2)
     // of the tile map, its map out + j out_tstride and its peak peak[j].
     // This block's k-th unit: see the kernel's comment for the two orders.
-    constexpr bool kRunning = MODE == kRunningMax || MODE == kRunningStats;
+    constexpr bool kRunning = MODE == kRunningMax || MODE == kRunningStats || MODE == kRunningSumSq;
     const int ngroups = (out_rows + C::RPB - 1) / C::RPB;
     const int units = ngroups * ntemplates;
     auto unit_of = [&](int k, int& tj, int& grp) -> bool {
@@ -803,10 +805,9 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
             const int yy = g0 + r;
             if (yy >= out_rows) break;
             prefetch_row(out + (size_t)yy * out_pitch, out_cols);
-            if constexpr (MODE == kRunningStats) {
-                prefetch_row(sum + (size_t)yy * out_pitch, out_cols);
+            if constexpr (MODE == kRunningStats) prefetch_row(sum + (size_t)yy * out_pitch, out_cols);
+            if constexpr (MODE == kRunningStats || MODE == kRunningSumSq)
                 prefetch_row(sumsq + (size_t)yy * out_pitch, out_cols);
-            }
         }
     };
 
@@ -993,12 +994,16 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                         }
                     }
                 }
-                if constexpr (MODE == kRunningStats) {
+                if constexpr (MODE == kRunningStats || MODE == kRunningSumSq) {
                     // Per-pixel sum and sum of squares (float accumulation);
                     // a chunk of a butterfly's outputs at a time, loads first.
-                    float* srow = sum + (size_t)y * out_pitch;
+                    // kRunningSumSq: the sum of squares alone (a caller can
+                    // get the sum of a batch's maps as the map of the batch's
+                    // summed template, correlation being linear).
+                    constexpr bool with_sum = MODE == kRunningStats;
+                    float* srow = with_sum ? sum + (size_t)y * out_pitch : nullptr;
                     float* qrow = sumsq + (size_t)y * out_pitch;
-                    const bool rvs = aligned8(srow) && aligned8(qrow);
+                    const bool rvs = (!with_sum || aligned8(srow)) && aligned8(qrow);
                     const bool fresh = (reset_j & (kResetMax | kResetSums)) != 0;
                     constexpr int SCH = largest_divisor_upto(RL, 4);
 #pragma unroll
@@ -1014,15 +1019,15 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                                 s1[i] = s2[i] = c_make(0.f, 0.f);
                                 if (!fresh) {
                                     if (rvs && 2 * m + 1 < out_cols) {
-                                        s1[i] = reinterpret_cast<const float2*>(srow)[m];
+                                        if constexpr (with_sum) s1[i] = reinterpret_cast<const float2*>(srow)[m];
                                         s2[i] = reinterpret_cast<const float2*>(qrow)[m];
                                     } else {
                                         if (2 * m < out_cols) {
-                                            s1[i].x = srow[2 * m];
+                                            if constexpr (with_sum) s1[i].x = srow[2 * m];
                                             s2[i].x = qrow[2 * m];
                                         }
                                         if (2 * m + 1 < out_cols) {
-                                            s1[i].y = srow[2 * m + 1];
+                                            if constexpr (with_sum) s1[i].y = srow[2 * m + 1];
                                             s2[i].y = qrow[2 * m + 1];
                                         }
                                     }
@@ -1036,15 +1041,15 @@ __global__ void __launch_bounds__(C2rCfg<W2>::THREADS, C2rCfg<W2>::MINB)
                                 const float2 b2 =
                                     c_make(fmaf(z.x, z.x, s2[i].x), fmaf(z.y, z.y, s2[i].y));
                                 if (rvs && 2 * m + 1 < out_cols) {
-                                    reinterpret_cast<float2*>(srow)[m] = a;
+                                    if constexpr (with_sum) reinterpret_cast<float2*>(srow)[m] = a;
                                     reinterpret_cast<float2*>(qrow)[m] = b2;
                                 } else {
                                     if (2 * m < out_cols) {
-                                        srow[2 * m] = a.x;
+                                        if constexpr (with_sum) srow[2 * m] = a.x;
                                         qrow[2 * m] = b2.x;
                                     }
                                     if (2 * m + 1 < out_cols) {
-                                        srow[2 * m + 1] = a.y;
+                                        if constexpr (with_sum) srow[2 * m + 1] = a.y;
                                         qrow[2 * m + 1] = b2.y;
                                     }
                                 }

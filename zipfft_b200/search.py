@@ -91,11 +91,26 @@ def _cuda_corr_max(batch, workspace, conv_data, max_map, arg_map, H, W, template
     stream = torch.cuda.current_stream(dev).cuda_stream
     lib = _lib.load()
     if sum_map is not None:
+        # Maximum, argmax and sum of squares per template; the batch's sum map
+        # is the correlation map of its summed template (correlation is
+        # linear): one more correlation per batch instead of a sum map read
+        # and written per template.
         st = lib.zfft_padded_real_corr_2d_max_stats(
             batch.data_ptr(), n, h, w, workspace.data_ptr(), workspace.numel() * 8,
-            conv_data.data_ptr(), max_map.data_ptr(), arg_map.data_ptr(), sum_map.data_ptr(),
+            conv_data.data_ptr(), max_map.data_ptr(), arg_map.data_ptr(), None,
             sumsq_map.data_ptr(), oy, ox, H, W, int(template_index_base), int(reset), dev,
             stream)
+        _lib.check(st)
+        summed = batch.sum(dim=0, keepdim=True, dtype=torch.float64).to(torch.float32)
+        fresh = int(reset) in (RESET_ALL, RESET_SUMS)
+        dst = sum_map if fresh else torch.empty_like(sum_map)
+        st = lib.zfft_padded_real_corr_2d(
+            summed.data_ptr(), 1, h, w, workspace.data_ptr(), workspace.numel() * 8,
+            conv_data.data_ptr(), dst.data_ptr(), oy, ox, H, W, dev, stream)
+        _lib.check(st)
+        if not fresh:
+            sum_map += dst
+        return
     else:
         st = lib.zfft_padded_real_corr_2d_max(
             batch.data_ptr(), n, h, w, workspace.data_ptr(), workspace.numel() * 8,
