@@ -305,6 +305,7 @@ def test_max_stats_without_sum_map_matches_with_it():
     lib = _lib.load()
     ws = torch.empty(B * lib.zfft_workspace_bytes(H, W) // 8, dtype=torch.complex64, device=dev)
     stream = torch.cuda.current_stream(0).cuda_stream
+    tm_d, spec_d = tm.to(dev), spec.to(dev)  # held: the calls below are asynchronous
     out = []
     for with_sum in (True, False):
         mx = torch.empty((H, W), device=dev)
@@ -312,7 +313,7 @@ def test_max_stats_without_sum_map_matches_with_it():
         sm = torch.zeros((H, W), device=dev)
         sq = torch.empty((H, W), device=dev)
         _lib.check(lib.zfft_padded_real_corr_2d_max_stats(
-            tm.to(dev).data_ptr(), B, h, w, ws.data_ptr(), ws.numel() * 8, spec.to(dev).data_ptr(),
+            tm_d.data_ptr(), B, h, w, ws.data_ptr(), ws.numel() * 8, spec_d.data_ptr(),
             mx.data_ptr(), am.data_ptr(), sm.data_ptr() if with_sum else None, sq.data_ptr(),
             H, W, H, W, 0, 1, 0, stream))
         torch.cuda.synchronize()
@@ -323,7 +324,7 @@ def test_max_stats_without_sum_map_matches_with_it():
 
     from zipfft_b200.search import template_search
 
-    mx, am, sm, sq = template_search(tm, spec.to(dev), H, W, batch_size=4, full=True, stats=True)
+    mx, am, sm, sq = template_search(tm, spec_d, H, W, batch_size=4, full=True, stats=True)
     ref = O.padded_corr2d_f64(tm.numpy(), spec.numpy(), H, W, True, True)
     scale = np.sqrt((ref ** 2).sum(axis=0).max())
     assert np.abs(sm.cpu().numpy() - ref.sum(axis=0)).max() / scale < 1e-5
