@@ -194,10 +194,11 @@ def template_search(templates: torch.Tensor, conv_data: torch.Tensor, fft_size_y
 
     stats=True: also the per-pixel sum and sum of squares of the correlations
     over all templates, for z-score normalisation; returns (max_map, arg_map,
-    sum_map, sumsq_map).  The kernels sum each batch in float32; the batches
-    (and the ranks, with one all-reduce) are added in float64, so the sums are
-    float64 and their rounding grows with the batch size, not with the
-    number of templates.
+    sum_map, sumsq_map).  Per batch, the kernels sum the squares in float32
+    and the batch's sum map is the correlation map of its summed template
+    (correlation is linear); the batches (and the ranks, with one all-reduce)
+    are added in float64, so the sums are float64 and their rounding grows
+    with the batch size, not with the number of templates.
 
     shard_base: `templates` is then only this rank's shard (each rank loads
     its own templates), its first template having global index shard_base;
